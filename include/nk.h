@@ -1,0 +1,259 @@
+/*
+ * nk.h — C ABI of libnk, the B200 (sm_100a) implementation of the
+ * nemotron-cutile-rs matrix-multiplication hot path.
+ *
+ * Each entry point replaces one function of the reference's Rust kernel
+ * wrappers (paths are within the nemotron-cutile-rs project).  The Rust side
+ * keeps its public API and swaps the body for an `extern "C"` call.
+ *
+ * Conventions
+ *   - Every function returns an nk_status.  NK_OK is 0.  On error, the
+ *     calling thread's nk_error_info (nk_last_error) holds the detail that
+ *     the matching Rust error variant carries.
+ *   - Validation order is the reference's: shape first, then argument
+ *     lengths in the reference's order.  Lengths are element counts
+ *     (the Rust slice / GpuTensor::numel values).
+ *   - Pointers named x, w, y, out, scores, ... are DEVICE pointers unless the
+ *     name ends in _host.  Calls are asynchronous on `stream` (a
+ *     cudaStream_t; NULL = the legacy default stream) unless stated.
+ *   - Conditions only the device can detect (a non-finite value during
+ *     quantization, an int4 code above 15, a kernel wait that timed out)
+ *     are reported by the functions that document a synchronisation, or
+ *     by nk_device_status().
+ *   - No entry point falls back to a CPU implementation.
+ */
+#ifndef NK_H
+#define NK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---------------------------------------------------------------- status */
+typedef int nk_status;
+enum {
+  NK_OK = 0,
+  NK_INVALID_SHAPE = 1,      /* GemmError::InvalidShape, QuantizeError/MoeRoutingError InvalidShape */
+  NK_LENGTH_MISMATCH = 2,    /* *::LengthMismatch{argument, expected, actual} */
+  NK_INVALID_PARAMS = 3,     /* QuantizeError::InvalidParams */
+  NK_INT4_OUT_OF_RANGE = 4,  /* QuantizeError::Int4OutOfRange(u8) */
+  NK_NON_FINITE_INPUT = 5,   /* QuantizeError::NonFiniteInput{index, value} */
+  NK_INVALID_ROW_COUNT = 6,  /* LinearError/MlpError/MoeError::InvalidRowCount */
+  NK_UNSUPPORTED = 7,        /* a layout/dtype combination libnk does not implement */
+  NK_DEVICE_ERROR = 8,       /* *::DeviceError(String) */
+  NK_TIMEOUT = 9,            /* a bounded device-side wait gave up */
+  NK_WORKSPACE_TOO_SMALL = 10
+};
+
+typedef struct nk_error_info {
+  int32_t code;
+  char argument[32];   /* LengthMismatch argument name ("lhs", "rhs", "output", ...) */
+  uint64_t expected;
+  uint64_t actual;
+  uint64_t index;      /* NonFiniteInput index */
+  float value;         /* NonFiniteInput value */
+  uint32_t byte_value; /* Int4OutOfRange value */
+  char message[256];   /* human-readable; DeviceError carries the CUDA error string */
+} nk_error_info;
+
+/* Copies the calling thread's last error into *out; returns its code. */
+nk_status nk_last_error(nk_error_info *out);
+/* Library version (major*10000 + minor*100 + patch). */
+int32_t nk_version(void);
+/* Synchronises `stream` and reports a device-side failure recorded by any
+ * libnk kernel on the current device since the last call (NK_TIMEOUT when a
+ * bounded wait gave up), then clears it. */
+nk_status nk_device_status(void *stream);
+
+/* dtypes of activations / outputs */
+enum { NK_F32 = 0, NK_BF16 = 1 };
+/* epilogue flags */
+enum { NK_EPI_RELU2 = 1 };
+
+/* ------------------------------------------------------------------ GEMM */
+
+/* Replaces nemotron_kernels::gemm::{gemm, gemm_into} (gemm.rs:318-363) and
+ * the host loop gemm_into_host (gemm.rs:91-112).
+ * C[M,N] = A[M,K] · B[K,N], f32 row-major, the reference layout, accumulated
+ * in f64 and rounded once to f32 like the host loop.  Validation follows
+ * validate_shape (gemm.rs:114-147): zero dim or overflow -> NK_INVALID_SHAPE,
+ * then lhs, rhs, output lengths -> NK_LENGTH_MISMATCH. Writes `out` in place. */
+nk_status nk_gemm_f32(const float *lhs, size_t lhs_len, const float *rhs, size_t rhs_len,
+                      float *out, size_t out_len, size_t m, size_t k, size_t n, void *stream);
+
+/* The projection GEMM behind LinearProjection::project_into
+ * (nemotron-nn/src/linear.rs:283-342), which Mamba2 in/out projections
+ * (mamba2.rs:229-263,353-359), attention Q/K/V/O (attention.rs:170-209) and the
+ * MLP/MoE experts (mlp.rs:201-208) call:
+ *   Y[M,N] = epilogue( X[M,K] · Wᵀ ),  W stored [N,K] (K contiguous).
+ * x_dtype: NK_BF16 or NK_F32 (f32 activations are split exactly into two
+ * bf16 halves, so the product keeps ~16 mantissa bits).  y_dtype: NK_BF16 or
+ * NK_F32.  bias: f32 [N] or NULL, added after the GEMM as linear.rs:333-339
+ * does.  flags: NK_EPI_RELU2 applies relu2 (activations.rs:68-71) after the
+ * bias, fusing mlp.rs:205.  Accumulation is f32 in tensor memory. */
+nk_status nk_gemm_bf16(const void *x, int32_t x_dtype, const uint16_t *w, const float *bias,
+                       void *y, int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
+                       void *stream);
+
+/* Same contract with int8 weights quantized per output row (symmetric absmax,
+ * nk_quantize_int8_row): W ≈ diag(scales) · wq, wq [N,K] int8, scales f32 [N].
+ * Dequantization happens inside the GEMM (codes are exact in bf16; the row
+ * scale is applied in the epilogue).  Not in the reference: it is the format
+ * the benchmark configurations name. */
+nk_status nk_gemm_w8row(const void *x, int32_t x_dtype, const int8_t *wq, const float *scales,
+                        const float *bias, void *y, int32_t y_dtype, int64_t m, int64_t k,
+                        int64_t n, int32_t flags, void *stream);
+
+/* Same contract with the reference's INT4-affine per-tensor weights
+ * (quantize.rs:131-204) in the reference's own linear layout: element (k, n)
+ * of the [K,N] = [input_dim, output_dim] matrix (linear.rs:324) has flat
+ * index k*N+n and lives in byte index/2, low nibble for even index
+ * (quantize.rs:59-81).  W = (code - zero_point) * scale, dequantized inside
+ * the GEMM.  Replaces the materialise-then-GEMM route of
+ * Int4LinearWeights::materialize_dense (linear.rs:126-131), which the
+ * reference's project() refuses (linear.rs:316-321).  packed_len must be
+ * ceil(K*N/2). */
+nk_status nk_gemm_w4a(const void *x, int32_t x_dtype, const uint8_t *packed, size_t packed_len,
+                      float scale, uint32_t zero_point, const float *bias, void *y,
+                      int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
+                      void *stream);
+
+/* -------------------------------------------------------------- quantize */
+
+/* quantize.rs:59-81 pack_int4_into_host.  Synchronises `stream` (the range
+ * check is a device reduction): NK_INT4_OUT_OF_RANGE reports the first value
+ * above 15, as the host loop does.  packed_len must be ceil(count/2). */
+nk_status nk_pack_int4(const uint8_t *values, size_t count, uint8_t *packed, size_t packed_len,
+                       void *stream);
+/* quantize.rs:89-120 unpack_int4_into_host. */
+nk_status nk_unpack_int4(const uint8_t *packed, size_t packed_len, size_t count, uint8_t *out,
+                         size_t out_len, void *stream);
+/* quantize.rs:131-144 quantize_int4_into_host: code = clamp(round_half_away(v/scale + zp), 0, 15).
+ * Synchronises `stream`: the first non-finite input is reported as
+ * NK_NON_FINITE_INPUT{index, value} and nothing is written, as the host
+ * loop returns before packing. */
+nk_status nk_quantize_int4(const float *values, size_t count, float scale, uint32_t zero_point,
+                           uint8_t *packed, size_t packed_len, void *stream);
+/* quantize.rs:156-178 dequantize_int4_into_host (and the async dequantize_int4,
+ * quantize.rs:333-349): out = (code - zp) * scale, f32. */
+nk_status nk_dequantize_int4(const uint8_t *packed, size_t packed_len, size_t count, float scale,
+                             uint32_t zero_point, float *out, size_t out_len, void *stream);
+/* quantize.rs:180-186 validate_int4_params (host only, no device work). */
+nk_status nk_validate_int4_params(float scale, uint32_t zero_point);
+/* Int8 per-output-row symmetric absmax quantization of W [N,K] f32:
+ * scales[n] = max|W[n,:]| / 127, wq = clamp(round_half_away(W/scale), -127, 127),
+ * an all-zero row gives scale 0 and codes 0.  Synchronises `stream`; a
+ * non-finite weight is reported as NK_NON_FINITE_INPUT.  Not in the
+ * reference (the benchmark configurations name this format). */
+nk_status nk_quantize_int8_row(const float *w, int64_t n, int64_t k, int8_t *wq, float *scales,
+                               void *stream);
+
+/* ---------------------------------------------------------------- routing */
+
+enum {
+  NK_ROUTE_SIGMOID = 0,        /* select_top_k, moe_routing.rs:168-186 (the reference router) */
+  NK_ROUTE_SOFTMAX = 1,        /* select_top_k_softmax, moe_routing.rs:188-216 */
+  NK_ROUTE_SIGMOID_RENORM = 2  /* sigmoid top-k, selected weights renormalised to sum 1
+                                  (the benchmark configuration; not in the reference) */
+};
+
+/* Replaces moe_route / moe_route_softmax (moe_routing.rs:499-532) and the
+ * host loops moe_route_into_host / moe_route_softmax_into_host
+ * (moe_routing.rs:118-166).  scores f32 [tokens, experts] row-major;
+ * indices int32 [tokens, top_k] (the reference's usize), weights f32.
+ * Ranking uses f32 total order, weight descending then expert index
+ * ascending, on sigmoid values computed as the reference computes them
+ * (the exponential is evaluated in double and rounded once to f32).
+ * Validation: experts == 0, top_k == 0 or top_k > experts -> NK_INVALID_SHAPE,
+ * then scores, indices, weights lengths.  tokens == 0 is valid and a no-op.
+ * The device kernel handles experts <= 1024 and top_k <= 32 (NK_UNSUPPORTED
+ * beyond). */
+nk_status nk_moe_route(const float *scores, size_t scores_len, size_t tokens, size_t experts,
+                       size_t top_k, int32_t mode, int32_t *indices, size_t indices_len,
+                       float *weights, size_t weights_len, void *stream);
+
+/* Expert histogram and permutation derived from routing indices (the
+ * reference has none: it runs every selected expert over all rows,
+ * moe.rs:226-233).  counts[e] = #{(t,r): indices[t*top_k+r] == e};
+ * offsets = exclusive prefix sum of counts (experts+1 entries, the last is
+ * tokens*top_k); perm[offsets[e] + j] = the j-th route slot t*top_k+r (in
+ * ascending slot order) that selected e; slot_pos[t*top_k+r] = its position
+ * in perm.  Deterministic.  Requires experts <= 1024. */
+nk_status nk_moe_plan(const int32_t *indices, int64_t tokens, int64_t top_k, int64_t experts,
+                      int32_t *counts, int32_t *offsets, int32_t *perm, int32_t *slot_pos,
+                      void *stream);
+
+/* -------------------------------------------------------------- MoE layer */
+
+enum { NK_W_BF16 = 0, NK_W_INT8_ROW = 1 };
+
+/* Weights of one MoE layer, all device pointers, in the layouts the B200
+ * kernels read (each GEMM weight is [out_features, in_features], K contiguous;
+ * nk_linear_pack_kn converts the reference's [in, out] layout).
+ * Expert tensors are stacked over experts. */
+typedef struct nk_moe_layer {
+  int64_t hidden;        /* H */
+  int64_t experts;       /* E */
+  int64_t top_k;         /* k */
+  int64_t inter;         /* I, routed expert width */
+  int64_t shared_inter;  /* Is, 0 = no shared expert */
+  int32_t route_mode;    /* NK_ROUTE_* */
+  int32_t weight_kind;   /* NK_W_BF16 or NK_W_INT8_ROW (experts and shared expert) */
+  const uint16_t *router_w3; /* [E, 3*Hp] bf16, Hp = ceil(H/64)*64: the f32 router weight
+                                [E,H] split exactly into three zero-padded bf16 parts
+                                (nk_router_split); scores carry f32 accuracy */
+  const float *router_b;     /* [E] or NULL */
+  const void *up_w;          /* [E, I, H] */
+  const float *up_scale;     /* [E, I] (INT8_ROW) */
+  const float *up_b;         /* [E, I] or NULL */
+  const void *down_w;        /* [E, H, I] */
+  const float *down_scale;   /* [E, H] (INT8_ROW) */
+  const float *down_b;       /* [E, H] or NULL */
+  const void *shared_up_w;   /* [Is, H] */
+  const float *shared_up_scale;
+  const float *shared_up_b;
+  const void *shared_down_w; /* [H, Is] */
+  const float *shared_down_scale;
+  const float *shared_down_b;
+} nk_moe_layer;
+
+/* Splits a router weight f32 [E,H] into the [E, 3*Hp] bf16 triple used by
+ * nk_moe_forward (hi | mid | lo, each zero padded to Hp = ceil(H/64)*64;
+ * hi + mid + lo == the f32 value for every normal f32). */
+nk_status nk_router_split(const float *router_w, int64_t experts, int64_t hidden,
+                          uint16_t *router_w3, void *stream);
+
+/* Converts a reference-layout linear weight f32 [K,N] (input_dim x output_dim,
+ * linear.rs:324) into the [N,K] bf16 layout the GEMMs read. */
+nk_status nk_linear_pack_kn(const float *w_kn, int64_t k, int64_t n, uint16_t *w_nk,
+                            void *stream);
+
+/* Device workspace (bytes) nk_moe_forward needs for `tokens` rows. */
+nk_status nk_moe_workspace_bytes(const nk_moe_layer *layer, int64_t tokens, size_t *bytes);
+
+/* Replaces MoeLayer::forward_into (nemotron-nn/src/moe.rs:154-249):
+ * router projection -> top-k routing -> per-expert MLP relu2(x·upᵀ)·downᵀ on
+ * the tokens routed to it (grouped GEMMs) -> out[t] = shared(x)[t] +
+ * Σ_r w[t,r]·expert_{idx[t,r]}(x)[t], summed in rank order in f32 like
+ * moe.rs:207-246.  x bf16 [tokens, H]; out [tokens, H] in out_dtype.
+ * indices/weights (int32/f32 [tokens, top_k]) receive the routing when not
+ * NULL.  workspace: device memory of nk_moe_workspace_bytes. */
+nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t tokens,
+                         void *out, int32_t out_dtype, int32_t *indices, float *weights,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NK_H */

@@ -1,0 +1,104 @@
+// common.cu — thread-local error record, per-device error word and scratch
+// arena, and the library-level entry points of nk.h.
+#include <mutex>
+#include <vector>
+
+#include "nk_common.cuh"
+
+namespace nk {
+
+nk_error_info &tls_error() {
+  static thread_local nk_error_info e{};
+  return e;
+}
+
+// One error word per device: kernels write NK_TIMEOUT / NK_DEVICE_ERROR here
+// instead of trapping.
+static __device__ int g_device_error;
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+int *g_err_ptr[kMaxDevices];
+void *g_scratch[kMaxDevices];
+size_t g_scratch_bytes[kMaxDevices];
+int g_sms[kMaxDevices];
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+}  // namespace
+
+int *device_error_ptr() {
+  int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_err_ptr[d]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    g_err_ptr[d] = static_cast<int *>(p);
+  }
+  return g_err_ptr[d];
+}
+
+int num_sms() {
+  int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return 148;
+  if (!g_sms[d]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
+    g_sms[d] = v > 0 ? v : 148;
+  }
+  return g_sms[d];
+}
+
+// The arena only grows.  Growth synchronises the device first so that no
+// queued kernel still uses the old block.
+nk_status scratch(size_t bytes, void **ptr, cudaStream_t) {
+  int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return fail(NK_DEVICE_ERROR, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_scratch_bytes[d] < bytes) {
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    if (g_scratch[d]) {
+      NK_CUDA_TRY(cudaDeviceSynchronize());
+      NK_CUDA_TRY(cudaFree(g_scratch[d]));
+      g_scratch[d] = nullptr;
+      g_scratch_bytes[d] = 0;
+    }
+    NK_CUDA_TRY(cudaMalloc(&g_scratch[d], want));
+    g_scratch_bytes[d] = want;
+  }
+  *ptr = g_scratch[d];
+  return NK_OK;
+}
+
+}  // namespace nk
+
+extern "C" {
+
+nk_status nk_last_error(nk_error_info *out) {
+  if (out) *out = nk::tls_error();
+  return nk::tls_error().code;
+}
+
+int32_t nk_version(void) { return 100; }
+
+nk_status nk_device_status(void *stream) {
+  NK_CUDA_TRY(cudaStreamSynchronize(nk::as_stream(stream)));
+  int *p = nk::device_error_ptr();
+  if (!p) return nk::fail(NK_DEVICE_ERROR, "cannot resolve device error word");
+  int v = 0;
+  NK_CUDA_TRY(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v != 0) {
+    int zero = 0;
+    NK_CUDA_TRY(cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    return nk::fail(v, v == NK_TIMEOUT ? "a bounded device-side wait timed out"
+                                       : "a device kernel reported an error");
+  }
+  return nk::ok();
+}
+
+}  // extern "C"

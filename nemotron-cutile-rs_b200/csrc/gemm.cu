@@ -1,0 +1,240 @@
+// gemm.cu — GEMM entry points of nk.h: the reference-layout f32 GEMM
+// (f64 accumulation, SIMT) and the projection GEMMs, which dispatch to the
+// tcgen05 kernel (gemm_tc.cu) or, for shapes TMA cannot address (a row pitch
+// that is not a multiple of 16 bytes), to a plain CUDA kernel.
+#include "gemm_tc.h"
+
+namespace nk {
+
+// ---------------------------------------------------------------- f32 GEMM
+// C[M,N] = A[M,K]·B[K,N] with f64 accumulation, rounded once to f32 — the
+// arithmetic of gemm_into_host (gemm.rs:99-109).  64x64 output tile, 256
+// threads, 4x4 outputs per thread, K staged 16 at a time through shared memory.
+__global__ void __launch_bounds__(256) gemm_f32_f64acc_kernel(const float *__restrict__ A,
+                                                              const float *__restrict__ B,
+                                                              float *__restrict__ C, int64_t M,
+                                                              int64_t K, int64_t N) {
+  __shared__ double As[16][64 + 1];
+  __shared__ double Bs[16][64 + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t row0 = (int64_t)blockIdx.y * 64, col0 = (int64_t)blockIdx.x * 64;
+  double acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < K; k0 += 16) {
+    for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+      int kk = e / 64, r = e % 64;  // A: element (row0+r, k0+kk)
+      int64_t gr = row0 + r, gk = k0 + kk;
+      As[kk][r] = (gr < M && gk < K) ? (double)A[gr * K + gk] : 0.0;
+      int64_t gc = col0 + r;  // B: element (k0+kk, col0+r), coalesced along N
+      Bs[kk][r] = (gk < K && gc < N) ? (double)B[gk * N + gc] : 0.0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      double a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t r = row0 + ty + 16 * i, c = col0 + tx + 16 * j;
+      if (r < M && c < N) C[r * N + c] = (float)acc[i][j];
+    }
+}
+
+// ------------------------------------------------------- projection helpers
+// Exact two-way split of f32 activations into bf16 hi | lo halves, written
+// as X2[m, 0:Kp] = hi, X2[m, Kp:2Kp] = lo (zero padded to Kp = ceil(K/64)*64).
+__global__ void split_f32_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ x2,
+                                 int64_t M, int64_t K, int64_t Kp) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= M * Kp) return;
+  int64_t m = idx / Kp, k = idx - m * Kp;
+  float v = k < K ? x[m * K + k] : 0.0f;
+  __nv_bfloat16 hi = __float2bfloat16_rn(v);
+  __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+  x2[m * 2 * Kp + k] = hi;
+  x2[m * 2 * Kp + Kp + k] = lo;
+}
+
+// Plain CUDA projection for shapes outside the TMA envelope: one thread per
+// output, f32 accumulation, the same epilogue as the tensor-core kernel.
+template <int WK>
+__global__ void proj_simt_kernel(const void *__restrict__ x, int x_f32,
+                                 const void *__restrict__ w, float w_scale, int zp,
+                                 const float *__restrict__ row_scale,
+                                 const float *__restrict__ bias, void *__restrict__ y, int y_f32,
+                                 int relu2, int64_t M, int64_t K, int64_t N) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= M * N) return;
+  int64_t m = idx / N, n = idx - m * N;
+  float acc = 0.0f;
+  for (int64_t k = 0; k < K; ++k) {
+    float xv = x_f32 ? reinterpret_cast<const float *>(x)[m * K + k]
+                     : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(x)[m * K + k]);
+    float wv;
+    if (WK == WK_BF16) {
+      wv = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(w)[n * K + k]);
+    } else if (WK == WK_INT8) {
+      wv = (float)reinterpret_cast<const int8_t *>(w)[n * K + k];
+    } else {
+      int64_t flat = k * N + n;  // reference [K,N] layout
+      uint8_t b = reinterpret_cast<const uint8_t *>(w)[flat >> 1];
+      wv = (float)((int)((flat & 1) ? (b >> 4) : (b & 0xF)) - zp);
+    }
+    acc = fmaf(xv, wv, acc);
+  }
+  float o = acc * w_scale;
+  if (row_scale) o *= row_scale[n];
+  if (bias) o += bias[n];
+  if (relu2) o = nk_relu2(o);
+  if (y_f32)
+    reinterpret_cast<float *>(y)[idx] = o;
+  else
+    reinterpret_cast<__nv_bfloat16 *>(y)[idx] = __float2bfloat16_rn(o);
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Shared driver for nk_gemm_bf16 / nk_gemm_w8row / nk_gemm_w4a.
+nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_scale, int zp,
+                     const float *row_scale, const float *bias, void *y, int y_dtype,
+                     int64_t m, int64_t k, int64_t n, int flags, cudaStream_t stream) {
+  if (m <= 0 || k <= 0 || n <= 0) return fail(NK_INVALID_SHAPE, "m, k and n must be positive");
+  if (x_dtype != NK_BF16 && x_dtype != NK_F32) return fail(NK_UNSUPPORTED, "x_dtype");
+  if (y_dtype != NK_BF16 && y_dtype != NK_F32) return fail(NK_UNSUPPORTED, "y_dtype");
+  if (m > (1ll << 30) || n > (1ll << 30) || k > (1ll << 30))
+    return fail(NK_INVALID_SHAPE, "dimension too large");
+  int *err = device_error_ptr();
+  const bool relu2 = (flags & NK_EPI_RELU2) != 0;
+
+  bool tc_ok = aligned16(x) && aligned16(w);
+  if (wk == WK_BF16) tc_ok &= (k % 8) == 0;
+  if (wk == WK_INT8) tc_ok &= (k % 16) == 0;
+  if (wk == WK_INT4KN) tc_ok &= (n % 32) == 0;
+  if (x_dtype == NK_BF16) tc_ok &= (k % 8) == 0;
+
+  if (!tc_ok) {
+    int64_t total = m * n;
+    int threads = 256;
+    int64_t blocks = (total + threads - 1) / threads;
+    if (wk == WK_BF16)
+      proj_simt_kernel<WK_BF16><<<(unsigned)blocks, threads, 0, stream>>>(
+          x, x_dtype == NK_F32, w, w_scale, zp, row_scale, bias, y, y_dtype == NK_F32, relu2, m,
+          k, n);
+    else if (wk == WK_INT8)
+      proj_simt_kernel<WK_INT8><<<(unsigned)blocks, threads, 0, stream>>>(
+          x, x_dtype == NK_F32, w, w_scale, zp, row_scale, bias, y, y_dtype == NK_F32, relu2, m,
+          k, n);
+    else
+      proj_simt_kernel<WK_INT4KN><<<(unsigned)blocks, threads, 0, stream>>>(
+          x, x_dtype == NK_F32, w, w_scale, zp, row_scale, bias, y, y_dtype == NK_F32, relu2, m,
+          k, n);
+    return check_launch("proj_simt_kernel");
+  }
+
+  const uint16_t *xb = reinterpret_cast<const uint16_t *>(x);
+  int64_t x_k = k, ldx = k;
+  int k_blocks = (int)ceil_div(k, 64);
+  int w_period = 0;
+  if (x_dtype == NK_F32) {
+    int64_t kp = ceil_div(k, 64) * 64;
+    void *buf = nullptr;
+    nk_status st = scratch((size_t)(m * 2 * kp * 2), &buf, stream);
+    if (st != NK_OK) return st;
+    int64_t total = m * kp;
+    split_f32_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, stream>>>(
+        reinterpret_cast<const float *>(x), reinterpret_cast<__nv_bfloat16 *>(buf), m, k, kp);
+    st = check_launch("split_f32_kernel");
+    if (st != NK_OK) return st;
+    xb = reinterpret_cast<const uint16_t *>(buf);
+    x_k = 2 * kp;
+    ldx = 2 * kp;
+    w_period = (int)(kp / 64);
+    k_blocks = 2 * w_period;
+  }
+
+  const int bn = m <= 64 ? 64 : 256;
+  TcArgs a{};
+  a.f_tiles = (int)ceil_div(n, 128);
+  a.t_tiles = (int)ceil_div(m, bn);
+  a.n_features = (int)n;
+  a.n_tokens = (int)m;
+  a.k_blocks = k_blocks;
+  a.w_k_period = w_period;
+  a.x_k_period = 0;
+  a.y = y;
+  a.ldy = n;
+  a.y_f32 = y_dtype == NK_F32;
+  a.w_scale = w_scale;
+  a.row_scale = row_scale;
+  a.bias = bias;
+  a.relu2 = relu2;
+  a.w_zero_point = zp;
+  a.err = err;
+  int64_t tiles = (int64_t)a.f_tiles * a.t_tiles;
+  int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  int64_t ldw_bytes = wk == WK_BF16 ? k * 2 : (wk == WK_INT8 ? k : n / 2);
+  return tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream);
+}
+
+}  // namespace nk
+
+using namespace nk;
+
+extern "C" {
+
+nk_status nk_gemm_f32(const float *lhs, size_t lhs_len, const float *rhs, size_t rhs_len,
+                      float *out, size_t out_len, size_t m, size_t k, size_t n, void *stream) {
+  uint64_t ll, rl, ol;
+  if (m == 0 || k == 0 || n == 0 || !mul_ok(m, k, &ll) || !mul_ok(k, n, &rl) ||
+      !mul_ok(m, n, &ol))
+    return fail(NK_INVALID_SHAPE, "invalid GEMM shape");
+  if (lhs_len != ll) return fail_length("lhs", ll, lhs_len);
+  if (rhs_len != rl) return fail_length("rhs", rl, rhs_len);
+  if (out_len != ol) return fail_length("output", ol, out_len);
+  dim3 grid((unsigned)ceil_div((int64_t)n, 64), (unsigned)ceil_div((int64_t)m, 64));
+  if (grid.y > 65535) return fail(NK_UNSUPPORTED, "m too large for one launch");
+  gemm_f32_f64acc_kernel<<<grid, 256, 0, as_stream(stream)>>>(lhs, rhs, out, (int64_t)m,
+                                                              (int64_t)k, (int64_t)n);
+  return check_launch("gemm_f32_f64acc_kernel");
+}
+
+nk_status nk_gemm_bf16(const void *x, int32_t x_dtype, const uint16_t *w, const float *bias,
+                       void *y, int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
+                       void *stream) {
+  return projection(WK_BF16, x, x_dtype, w, 1.0f, 0, nullptr, bias, y, y_dtype, m, k, n, flags,
+                    as_stream(stream));
+}
+
+nk_status nk_gemm_w8row(const void *x, int32_t x_dtype, const int8_t *wq, const float *scales,
+                        const float *bias, void *y, int32_t y_dtype, int64_t m, int64_t k,
+                        int64_t n, int32_t flags, void *stream) {
+  return projection(WK_INT8, x, x_dtype, wq, 1.0f, 0, scales, bias, y, y_dtype, m, k, n, flags,
+                    as_stream(stream));
+}
+
+nk_status nk_gemm_w4a(const void *x, int32_t x_dtype, const uint8_t *packed, size_t packed_len,
+                      float scale, uint32_t zero_point, const float *bias, void *y,
+                      int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
+                      void *stream) {
+  if (m <= 0 || k <= 0 || n <= 0) return fail(NK_INVALID_SHAPE, "m, k and n must be positive");
+  nk_status st = nk_validate_int4_params(scale, zero_point);
+  if (st != NK_OK) return st;
+  uint64_t count = (uint64_t)k * (uint64_t)n;
+  uint64_t expect = count / 2 + (count & 1);
+  if (packed_len != expect) return fail_length("packed_weights", expect, packed_len);
+  return projection(WK_INT4KN, x, x_dtype, packed, scale, (int)zero_point, nullptr, bias, y,
+                    y_dtype, m, k, n, flags, as_stream(stream));
+}
+
+}  // extern "C"

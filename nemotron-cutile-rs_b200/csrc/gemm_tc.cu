@@ -1,0 +1,399 @@
+// gemm_tc.cu — the warp-specialised tcgen05 projection GEMM (see gemm_tc.cuh)
+// and its host launcher.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm_tc.cuh"
+
+namespace nk {
+
+template <int BN>
+__device__ __forceinline__ bool load_tile(const TcArgs &a, int t, TcTile &tile) {
+  if (a.tiles) {
+    tile = a.tiles[t];
+    return true;
+  }
+  int ft = t / a.t_tiles, tt = t - ft * a.t_tiles;
+  tile.w_row = ft * 128;
+  tile.x_row = tt * BN;
+  tile.out_col0 = ft * 128;
+  int fv = a.n_features - ft * 128;
+  int tv = a.n_tokens - tt * BN;
+  tile.valid = ((fv > 128 ? 128 : fv) << 16) | (tv > BN ? BN : tv);
+  return true;
+}
+
+template <int WK, int BN>
+__global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+                   const __grid_constant__ CUtensorMap xmap, const TcArgs args) {
+  using Cfg = TcConfig<WK, BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *a_tiles = smem;                               // S x 16 KB (bf16, SW128)
+  uint8_t *b_tiles = a_tiles + S * Cfg::kABytes;         // S x BN*128
+  uint8_t *raw_tiles = b_tiles + S * Cfg::kBBytes;       // S x raw weight tile
+  uint64_t *bars = reinterpret_cast<uint64_t *>(raw_tiles + S * Cfg::kRawBytes);
+  uint64_t *full = bars;            // TMA landed (weights raw/direct + activations)
+  uint64_t *empty = bars + S;       // MMA finished reading the stage
+  uint64_t *conv = bars + 2 * S;    // transform finished (quantized weights)
+  uint64_t *tfull = bars + 3 * S;   // accumulator ready (2)
+  uint64_t *tempty = bars + 3 * S + 2;  // accumulator drained (2)
+  uint64_t *drain = bars + 3 * S + 4;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int *err = args.err;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&wmap);
+    tma_prefetch_desc(&xmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.tiles ? *args.tile_count : args.f_tiles * args.t_tiles;
+  volatile int *abort_v = &abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        TcTile tile;
+        load_tile<BN>(args, t, tile);
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (*abort_v || !mbar_wait(&empty[stage], phase ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
+          int xkb = args.x_k_period > 0 ? kb % args.x_k_period : kb;
+          mbar_arrive_expect_tx(&full[stage], (WK == WK_BF16 ? Cfg::kABytes : Cfg::kRawBytes) +
+                                                  Cfg::kBBytes);
+          if (WK == WK_BF16)
+            tma_load_2d(a_tiles + stage * Cfg::kABytes, &wmap, &full[stage], wkb * 64,
+                        tile.w_row);
+          else if (WK == WK_INT8)
+            tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &full[stage], wkb * 64,
+                        tile.w_row);
+          else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
+            tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &full[stage],
+                        tile.w_row >> 1, wkb * 64);
+          tma_load_2d(b_tiles + stage * Cfg::kBBytes, &xmap, &full[stage], xkb * 64, tile.x_row);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) *abort_v = 1;
+      // Drain: every issued load must have landed before the CTA may exit.
+      for (int s = 0; s < S; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1, err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(a_tiles), b_base = smem_u32(b_tiles);
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        TcTile tile;
+        load_tile<BN>(args, t, tile);
+        int t_valid = tile.valid & 0xFFFF;
+        uint32_t n_mma = (uint32_t)((t_valid + 15) & ~15);
+        if (n_mma < 16) n_mma = 16;
+        if (n_mma > BN) n_mma = BN;
+        const uint32_t idesc = idesc_bf16_f32(128, n_mma);
+        if (*abort_v || !mbar_wait(&tempty[acc], acc_phase ^ 1, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          bool got = WK == WK_BF16 ? mbar_wait(&full[stage], phase, err)
+                                   : mbar_wait(&conv[stage], phase, err);
+          if (*abort_v || !got) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint64_t ad = smem_desc_sw128(a_base + stage * Cfg::kABytes);
+          uint64_t bd = smem_desc_sw128(b_base + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)  // 4 x K=16 steps, +32 bytes each (encoded >>4: +2)
+            tc_mma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+          tc_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) *abort_v = 1;
+      // Drain: all issued MMAs complete before TMEM is released.
+      tc_commit(drain);
+      mbar_wait(drain, 0, err);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
+    const int i = quarter * 32 + lane;  // feature row within the tile
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      TcTile tile;
+      load_tile<BN>(args, t, tile);
+      const int f_valid = tile.valid >> 16, t_valid = tile.valid & 0xFFFF;
+      // warp-uniform decision: tcgen05.ld below is .sync.aligned
+      const bool stop = __any_sync(0xffffffffu, *abort_v || !mbar_wait(&tfull[acc], acc_phase, err));
+      if (stop) {
+        *abort_v = 1;
+        break;
+      }
+      tc_fence_after();
+      const bool frow = i < f_valid;
+      const int f = tile.w_row + i;
+      float mul = args.w_scale, add = 0.0f;
+      if (frow) {
+        if (args.row_scale) mul *= args.row_scale[f];
+        if (args.bias) add = args.bias[f];
+      }
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      const int chunks = (t_valid + 15) >> 4;
+      for (int c = 0; c < chunks; ++c) {
+        float v[16];
+        tmem_ld16(taddr + c * 16, v);
+        if (frow) {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = c * 16 + jj;
+            if (j < t_valid) {
+              float o = v[jj] * mul + add;
+              if (args.relu2) o = nk_relu2(o);
+              if (args.tok_scale) o *= args.tok_scale[tile.x_row + j];
+              const long long off =
+                  (long long)(tile.x_row + j) * args.ldy + tile.out_col0 + i;
+              if (args.y_f32)
+                reinterpret_cast<float *>(args.y)[off] = o;
+              else
+                reinterpret_cast<__nv_bfloat16 *>(args.y)[off] = __float2bfloat16_rn(o);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  } else if (WK != WK_BF16) {
+    // ------------------------------------------------------------ transform
+    const int tid = threadIdx.x - 192;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (*abort_v || !mbar_wait(&full[stage], phase, err)) {
+          ok = false;
+          break;
+        }
+        const uint8_t *raw = raw_tiles + stage * Cfg::kRawBytes;
+        uint8_t *dst = a_tiles + stage * Cfg::kABytes;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int idx = q * 128 + tid;
+          int row, c;
+          uint32_t packed[4];
+          if (WK == WK_INT8) {
+            row = idx >> 3;
+            c = idx & 7;
+            const uint2 src = *reinterpret_cast<const uint2 *>(raw + row * 64 + c * 8);
+            const uint32_t w[2] = {src.x, src.y};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const uint32_t word = w[h >> 1];
+              const int sh = (h & 1) * 16;
+              float lo = (float)(int8_t)((word >> sh) & 0xFF);
+              float hi = (float)(int8_t)((word >> (sh + 8)) & 0xFF);
+              __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+              packed[h] = *reinterpret_cast<uint32_t *>(&p);
+            }
+          } else {  // INT4 [K][128 features as 64 bytes]: element (k, n) -> byte k*64 + n/2
+            row = idx & 127;  // feature
+            c = idx >> 7;     // K chunk of 8
+            const int sh = (row & 1) * 4;
+            float vals[8];
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint8_t b = raw[(c * 8 + kk) * 64 + (row >> 1)];
+              vals[kk] = (float)((int)((b >> sh) & 0xF) - args.w_zero_point);
+            }
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              __nv_bfloat162 p = __floats2bfloat162_rn(vals[2 * h], vals[2 * h + 1]);
+              packed[h] = *reinterpret_cast<uint32_t *>(&p);
+            }
+          }
+          *reinterpret_cast<uint4 *>(dst + row * 128 + ((c ^ (row & 7)) << 4)) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) {
+        *abort_v = 1;
+        break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace nk
+
+// ======================================================================= host
+namespace nk {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor map: `cols` contiguous elements per row, `rows` rows,
+// `row_bytes` between rows; box = box_cols x box_rows.
+nk_status make_map(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes, const void *base,
+                   uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t box_cols,
+                   uint32_t box_rows, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return fail(NK_DEVICE_ERROR, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15))
+    return fail(NK_UNSUPPORTED, "TMA needs 16-byte aligned base and row pitch");
+  (void)elem_bytes;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[128];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return fail(NK_DEVICE_ERROR, buf);
+  }
+  return NK_OK;
+}
+
+template <int WK, int BN>
+nk_status launch_impl(const CUtensorMap &wm, const CUtensorMap &xm, const TcArgs &args, int grid,
+                      cudaStream_t stream) {
+  using Cfg = TcConfig<WK, BN>;
+  static bool attr_done = false;  // benign race: setting the attribute twice is harmless
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WK, BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(tc_gemm)");
+    attr_done = true;
+  }
+  tc_gemm_kernel<WK, BN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(wm, xm, args);
+  return check_launch("tc_gemm_kernel");
+}
+
+}  // namespace
+
+// See gemm_tc.h.  w: bf16 [n_w_rows, ldw] / int8 [n_w_rows, ldw] / int4 bytes [K, N/2].
+nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ldw_bytes,
+                  const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
+                  TcArgs args, int grid, cudaStream_t stream) {
+  CUtensorMap wm, xm;
+  nk_status st;
+  if (wk == WK_BF16)
+    st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, (uint64_t)w_k, (uint64_t)w_rows,
+                  (uint64_t)ldw_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  else if (wk == WK_INT8)
+    st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)w_k, (uint64_t)w_rows,
+                  (uint64_t)ldw_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else  // INT4 reference layout: rows = K, cols = N/2 bytes
+    st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)(w_rows / 2),
+                  (uint64_t)w_k, (uint64_t)ldw_bytes, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != NK_OK) return st;
+  st = make_map(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)x_k, (uint64_t)x_rows,
+                (uint64_t)ldx_elems * 2, 64, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NK_OK) return st;
+  if (grid <= 0) return ok();
+  if (wk == WK_BF16)
+    return bn == 256 ? launch_impl<WK_BF16, 256>(wm, xm, args, grid, stream)
+                     : launch_impl<WK_BF16, 64>(wm, xm, args, grid, stream);
+  if (wk == WK_INT8)
+    return bn == 256 ? launch_impl<WK_INT8, 256>(wm, xm, args, grid, stream)
+                     : launch_impl<WK_INT8, 64>(wm, xm, args, grid, stream);
+  return bn == 256 ? launch_impl<WK_INT4KN, 256>(wm, xm, args, grid, stream)
+                   : launch_impl<WK_INT4KN, 64>(wm, xm, args, grid, stream);
+}
+
+}  // namespace nk

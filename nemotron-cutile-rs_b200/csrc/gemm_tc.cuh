@@ -1,0 +1,80 @@
+// gemm_tc.cuh — the sm_100a projection GEMM shared by every libnk entry point.
+//
+//   D[f, t] = Σ_k W[f, k] · X[t, k]          (tcgen05.mma, f32 accumulators in TMEM)
+//   Y[t, out_col0 + f] = epilogue(D[f, t])   (stored transposed: Y is [tokens, features])
+//
+// The weight operand is always the MMA "A" side (128 feature rows per tile)
+// and the activations the "B" side (up to BN token rows per tile), so one
+// kernel serves decode (a handful of tokens: N of the MMA shrinks to 16) and
+// prefill, dense and grouped (MoE) alike.  Weights come as bf16 [N,K], int8
+// [N,K] (per-row scale) or the reference's INT4-affine [K,N] nibble layout;
+// the quantized kinds are dequantized inside the kernel by "transform"
+// warps that turn the raw TMA tile into the bf16 128-byte-swizzled tile the
+// tensor core reads.
+//
+// Warp roles (one CTA per SM, persistent over a tile list):
+//   warp 0      TMA producer (one lane)
+//   warp 1      TMEM allocator + MMA issuer (one lane)
+//   warps 2-5   epilogue: TMEM -> registers -> scale/bias/relu2/token weight -> global
+//   warps 6-9   transform (quantized weights only)
+// Every mbarrier wait is bounded (mbar_wait); on a timeout the kernel records
+// NK_TIMEOUT, drains its own TMA loads and MMAs, frees TMEM and returns.
+#pragma once
+
+#include <cuda.h>
+
+#include "nk_common.cuh"
+#include "nk_ptx.cuh"
+
+namespace nk {
+
+enum WeightKind { WK_BF16 = 0, WK_INT8 = 1, WK_INT4KN = 2 };
+
+struct TcTile {  // one output tile: 128 features x up to BN tokens
+  int w_row;     // first weight row (feature) in the weight tensor map
+  int x_row;     // first activation row in the activation tensor map
+  int valid;     // (f_valid << 16) | t_valid
+  int out_col0;  // output column of feature 0 of the tile
+};
+
+struct TcArgs {
+  // tile list: dense grid (tiles == nullptr) or an explicit list
+  int f_tiles, t_tiles;     // dense: features N in 128-row tiles, tokens M in BN-row tiles
+  int n_features, n_tokens; // dense extents
+  const TcTile *tiles;      // grouped: list written by a device kernel
+  const int *tile_count;    // grouped: number of valid entries in `tiles`
+  int k_blocks;             // 64-wide K blocks of the contraction
+  int w_k_period;           // >0: weight K block = kb % w_k_period
+  int x_k_period;           // >0: activation K block = kb % x_k_period
+  // epilogue
+  void *y;
+  long long ldy;
+  int y_f32;
+  float w_scale;            // per-tensor weight scale (INT4); 1 otherwise
+  const float *row_scale;   // [features] per weight row (INT8 row scale) or null
+  const float *bias;        // [features] or null
+  const float *tok_scale;   // [activation rows] per token (routing weight) or null
+  int relu2;
+  int w_zero_point;         // INT4 zero point
+  int *err;
+};
+
+template <int WK>
+struct WeightTile {
+  static constexpr int kRawBytes = WK == WK_BF16 ? 0 : (WK == WK_INT8 ? 128 * 64 : 64 * 64);
+};
+
+template <int WK, int BN>
+struct TcConfig {
+  static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
+  static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
+  static constexpr int kRawBytes = WeightTile<WK>::kRawBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+  static constexpr int kStages0 = (224 * 1024) / kStageBytes;
+  static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+  static constexpr int kThreads = WK == WK_BF16 ? 192 : 320;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
+};
+
+}  // namespace nk

@@ -1,0 +1,16 @@
+// gemm_tc.h — host interface of the tcgen05 projection GEMM.
+#pragma once
+#include "gemm_tc.cuh"
+
+namespace nk {
+
+// Launches tc_gemm_kernel.  Weight operand (A): wk = WK_BF16 / WK_INT8 with
+// w_rows feature rows of w_k elements, row pitch ldw_bytes; or WK_INT4KN with
+// the reference [K,N] nibble layout (w_rows = N features, w_k = K rows,
+// ldw_bytes = N/2).  Activations (B): bf16 [x_rows, x_k], pitch ldx_elems.
+// bn: 256 or 64 token rows per tile.  grid: CTAs (persistent over tiles).
+nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ldw_bytes,
+                  const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
+                  TcArgs args, int grid, cudaStream_t stream);
+
+}  // namespace nk

@@ -1,0 +1,332 @@
+"""nk.py — Python binding of libnk's C ABI (include/nk.h) over ctypes.
+
+Device memory, streams and process groups come from PyTorch; every compute
+call goes through libnk.so (sm_100a kernels).  There is no CPU path: when
+libnk.so is missing or no GPU is present, calls raise.
+
+The wrappers mirror the reference's kernel-wrapper API
+(nemotron-kernels/src/{gemm,quantize,moe_routing}.rs): same argument order
+and the same error variants, raised as NkError with the variant's payload.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnk.so")
+
+# status codes (nk.h)
+OK, INVALID_SHAPE, LENGTH_MISMATCH, INVALID_PARAMS, INT4_OUT_OF_RANGE = 0, 1, 2, 3, 4
+NON_FINITE_INPUT, INVALID_ROW_COUNT, UNSUPPORTED, DEVICE_ERROR, TIMEOUT = 5, 6, 7, 8, 9
+WORKSPACE_TOO_SMALL = 10
+STATUS_NAMES = {
+    0: "Ok", 1: "InvalidShape", 2: "LengthMismatch", 3: "InvalidParams",
+    4: "Int4OutOfRange", 5: "NonFiniteInput", 6: "InvalidRowCount", 7: "Unsupported",
+    8: "DeviceError", 9: "Timeout", 10: "WorkspaceTooSmall",
+}
+F32, BF16 = 0, 1
+EPI_RELU2 = 1
+ROUTE_SIGMOID, ROUTE_SOFTMAX, ROUTE_SIGMOID_RENORM = 0, 1, 2
+W_BF16, W_INT8_ROW = 0, 1
+
+_c = ctypes
+_sz = _c.c_size_t
+_i64 = _c.c_int64
+_i32 = _c.c_int32
+_u32 = _c.c_uint32
+_p = _c.c_void_p
+_f = _c.c_float
+
+
+class NkErrorInfo(_c.Structure):
+    _fields_ = [
+        ("code", _c.c_int32),
+        ("argument", _c.c_char * 32),
+        ("expected", _c.c_uint64),
+        ("actual", _c.c_uint64),
+        ("index", _c.c_uint64),
+        ("value", _c.c_float),
+        ("byte_value", _c.c_uint32),
+        ("message", _c.c_char * 256),
+    ]
+
+
+class NkMoeLayer(_c.Structure):
+    _fields_ = [
+        ("hidden", _i64), ("experts", _i64), ("top_k", _i64), ("inter", _i64),
+        ("shared_inter", _i64), ("route_mode", _i32), ("weight_kind", _i32),
+        ("router_w3", _p), ("router_b", _p),
+        ("up_w", _p), ("up_scale", _p), ("up_b", _p),
+        ("down_w", _p), ("down_scale", _p), ("down_b", _p),
+        ("shared_up_w", _p), ("shared_up_scale", _p), ("shared_up_b", _p),
+        ("shared_down_w", _p), ("shared_down_scale", _p), ("shared_down_b", _p),
+    ]
+
+
+class NkError(Exception):
+    """A libnk status other than NK_OK, with the matching Rust variant's payload."""
+
+    def __init__(self, info: NkErrorInfo):
+        self.code = int(info.code)
+        self.variant = STATUS_NAMES.get(self.code, str(self.code))
+        self.argument = info.argument.decode()
+        self.expected = int(info.expected)
+        self.actual = int(info.actual)
+        self.index = int(info.index)
+        self.value = float(info.value)
+        self.byte_value = int(info.byte_value)
+        self.message = info.message.decode(errors="replace")
+        super().__init__(f"{self.variant}: {self.message}")
+
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "nk_last_error": (_i32, [_p]),
+    "nk_version": (_i32, []),
+    "nk_device_status": (_i32, [_p]),
+    "nk_gemm_f32": (_i32, [_p, _sz, _p, _sz, _p, _sz, _sz, _sz, _sz, _p]),
+    "nk_gemm_bf16": (_i32, [_p, _i32, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
+    "nk_gemm_w8row": (_i32, [_p, _i32, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
+    "nk_gemm_w4a": (_i32, [_p, _i32, _p, _sz, _f, _u32, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
+    "nk_pack_int4": (_i32, [_p, _sz, _p, _sz, _p]),
+    "nk_unpack_int4": (_i32, [_p, _sz, _sz, _p, _sz, _p]),
+    "nk_quantize_int4": (_i32, [_p, _sz, _f, _u32, _p, _sz, _p]),
+    "nk_dequantize_int4": (_i32, [_p, _sz, _sz, _f, _u32, _p, _sz, _p]),
+    "nk_validate_int4_params": (_i32, [_f, _u32]),
+    "nk_quantize_int8_row": (_i32, [_p, _i64, _i64, _p, _p, _p]),
+    "nk_moe_route": (_i32, [_p, _sz, _sz, _sz, _sz, _i32, _p, _sz, _p, _sz, _p]),
+    "nk_moe_plan": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
+    "nk_router_split": (_i32, [_p, _i64, _i64, _p, _p]),
+    "nk_linear_pack_kn": (_i32, [_p, _i64, _i64, _p, _p]),
+    "nk_moe_workspace_bytes": (_i32, [_p, _i64, _p]),
+    "nk_moe_forward": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libnk.so (built in-tree by `make -C nemotron-cutile-rs_b200`)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libnk.so not built: {LIB_PATH} (run make -C {_HERE})")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def last_error() -> NkErrorInfo:
+    info = NkErrorInfo()
+    lib().nk_last_error(ctypes.byref(info))
+    return info
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise NkError(last_error())
+
+
+def call(name: str, *args) -> None:
+    """Calls an nk_* entry point and raises NkError on a non-OK status."""
+    check(getattr(lib(), name)(*args))
+
+
+# ----------------------------------------------------------------- torch glue
+def ptr(t) -> int | None:
+    """Device address of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream=None) -> int:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("libnk entry points take device tensors")
+
+
+def bf16_bits(t):
+    """View a bf16 tensor's storage for the uint16_t* parameters."""
+    return t
+
+
+# ------------------------------------------------------------ kernel wrappers
+def gemm_f32(lhs, rhs, m: int, k: int, n: int, out=None, stream=None):
+    """nemotron_kernels::gemm::gemm / gemm_into (gemm.rs:318-363)."""
+    import torch
+
+    _require_cuda(lhs, rhs, out)
+    if out is None:
+        out = torch.empty(m * n if m * n > 0 else 1, dtype=torch.float32, device=lhs.device)
+        out_len = m * n
+    else:
+        out_len = out.numel()
+    call("nk_gemm_f32", ptr(lhs), lhs.numel(), ptr(rhs), rhs.numel(), ptr(out), out_len,
+         m, k, n, stream_ptr(stream))
+    return out
+
+
+def gemm(x, w, *, kind: str = "bf16", bias=None, scales=None, scale: float = 1.0,
+         zero_point: int = 0, n: int | None = None, out_dtype=None, relu2: bool = False,
+         stream=None):
+    """Projection Y[M,N] = X[M,K]·Wᵀ (+bias) (relu2) — LinearProjection::project_into.
+
+    kind: "bf16" (w bf16 [N,K]), "int8" (w int8 [N,K], scales f32 [N]),
+    "int4" (w uint8 packed reference layout [K,N], scale/zero_point).
+    """
+    import torch
+
+    _require_cuda(x, w, bias, scales)
+    m, k = x.shape
+    x_dtype = F32 if x.dtype == torch.float32 else BF16
+    if kind == "int4":
+        assert n is not None
+    else:
+        n = w.shape[0]
+    out_dtype = out_dtype or torch.float32
+    y = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    y_dtype = F32 if out_dtype == torch.float32 else BF16
+    flags = EPI_RELU2 if relu2 else 0
+    s = stream_ptr(stream)
+    if kind == "bf16":
+        call("nk_gemm_bf16", ptr(x), x_dtype, ptr(w), ptr(bias), ptr(y), y_dtype, m, k, n, flags, s)
+    elif kind == "int8":
+        call("nk_gemm_w8row", ptr(x), x_dtype, ptr(w), ptr(scales), ptr(bias), ptr(y), y_dtype,
+             m, k, n, flags, s)
+    elif kind == "int4":
+        call("nk_gemm_w4a", ptr(x), x_dtype, ptr(w), w.numel(), float(scale), int(zero_point),
+             ptr(bias), ptr(y), y_dtype, m, k, n, flags, s)
+    else:
+        raise ValueError(kind)
+    return y
+
+
+def moe_route(scores, tokens: int, experts: int, top_k: int, mode: int = ROUTE_SIGMOID,
+              stream=None):
+    """moe_routing::moe_route / moe_route_softmax (moe_routing.rs:499-532)."""
+    import torch
+
+    _require_cuda(scores)
+    dev = scores.device
+    n = max(tokens * top_k, 1)
+    idx = torch.empty(n, dtype=torch.int32, device=dev)
+    w = torch.empty(n, dtype=torch.float32, device=dev)
+    call("nk_moe_route", ptr(scores), scores.numel(), tokens, experts, top_k, mode, ptr(idx),
+         tokens * top_k, ptr(w), tokens * top_k, stream_ptr(stream))
+    return idx[: tokens * top_k], w[: tokens * top_k]
+
+
+def moe_plan(indices, tokens: int, top_k: int, experts: int, stream=None):
+    import torch
+
+    dev = indices.device
+    slots = tokens * top_k
+    counts = torch.empty(experts, dtype=torch.int32, device=dev)
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(max(slots, 1), dtype=torch.int32, device=dev)
+    pos = torch.empty(max(slots, 1), dtype=torch.int32, device=dev)
+    call("nk_moe_plan", ptr(indices), tokens, top_k, experts, ptr(counts), ptr(offsets),
+         ptr(perm), ptr(pos), stream_ptr(stream))
+    return counts, offsets, perm[:slots], pos[:slots]
+
+
+def quantize_int8_row(w, stream=None):
+    import torch
+
+    n, k = w.shape
+    q = torch.empty((n, k), dtype=torch.int8, device=w.device)
+    s = torch.empty(n, dtype=torch.float32, device=w.device)
+    call("nk_quantize_int8_row", ptr(w), n, k, ptr(q), ptr(s), stream_ptr(stream))
+    return q, s
+
+
+def router_split(w, stream=None):
+    import torch
+
+    e, h = w.shape
+    hp = (h + 63) // 64 * 64
+    w3 = torch.empty((e, 3 * hp), dtype=torch.bfloat16, device=w.device)
+    call("nk_router_split", ptr(w), e, h, ptr(w3), stream_ptr(stream))
+    return w3
+
+
+@dataclass
+class MoeWeights:
+    """Device tensors of one MoE layer in libnk's layouts (see nk_moe_layer)."""
+    hidden: int
+    experts: int
+    top_k: int
+    inter: int
+    shared_inter: int
+    route_mode: int
+    weight_kind: int
+    router_w3: object
+    router_b: object = None
+    up_w: object = None
+    up_scale: object = None
+    up_b: object = None
+    down_w: object = None
+    down_scale: object = None
+    down_b: object = None
+    shared_up_w: object = None
+    shared_up_scale: object = None
+    shared_up_b: object = None
+    shared_down_w: object = None
+    shared_down_scale: object = None
+    shared_down_b: object = None
+
+    def struct(self) -> NkMoeLayer:
+        s = NkMoeLayer()
+        for f in ("hidden", "experts", "top_k", "inter", "shared_inter", "route_mode",
+                  "weight_kind"):
+            setattr(s, f, getattr(self, f))
+        for f in ("router_w3", "router_b", "up_w", "up_scale", "up_b", "down_w", "down_scale",
+                  "down_b", "shared_up_w", "shared_up_scale", "shared_up_b", "shared_down_w",
+                  "shared_down_scale", "shared_down_b"):
+            setattr(s, f, ptr(getattr(self, f)))
+        return s
+
+
+class MoeLayer:
+    """Device MoE layer: MoeLayer::forward_into (nemotron-nn/src/moe.rs:154-249)."""
+
+    def __init__(self, weights: MoeWeights):
+        self.weights = weights
+        self._struct = weights.struct()
+        self._ws = None
+
+    def workspace_bytes(self, tokens: int) -> int:
+        b = ctypes.c_size_t(0)
+        call("nk_moe_workspace_bytes", ctypes.byref(self._struct), tokens, ctypes.byref(b))
+        return b.value
+
+    def forward(self, x, out=None, out_dtype=None, indices=None, weights=None, stream=None):
+        import torch
+
+        t = x.shape[0]
+        need = self.workspace_bytes(t)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty((t, self.weights.hidden), dtype=out_dtype or torch.float32,
+                              device=x.device)
+        od = F32 if out.dtype == torch.float32 else BF16
+        call("nk_moe_forward", ctypes.byref(self._struct), ptr(x), t, ptr(out), od, ptr(indices),
+             ptr(weights), ptr(self._ws), self._ws.numel(), stream_ptr(stream))
+        return out
+
+
+def device_status(stream=None) -> None:
+    call("nk_device_status", stream_ptr(stream))
