@@ -1,0 +1,403 @@
+"""bench.py — MoE layer throughput through libnk on B200.
+
+A step is one MoeLayer forward (router GEMM -> top-6 routing -> grouped expert
+GEMMs -> shared expert -> combine) over T=4096 tokens per GPU, hidden 2688,
+128 experts of width 1856, shared expert 3712, bf16 weights ~ N(0, 0.02),
+activations ~ N(0, 1), seeded synthetic data.  Weak scaling: every rank runs
+its own 4096 tokens.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nk|reference]
+                    [--weights bf16|int8]
+
+`--impl reference` times the reference's CPU algorithm (the committed C
+restatement in oracle/, since the Rust reference cannot be built here) on
+all host cores, over a bounded token sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nemotron-cutile-rs_b200"))
+
+METRIC = "grouped/quantized GEMM TFLOP/s (% tensor peak) & MoE tokens/s at 1-8 B200"
+T, H, E, K, I, IS = 4096, 2688, 128, 6, 1856, 3712
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        d["source"] = "measured"
+        return d
+    d = dict(FALLBACK_PEAKS)
+    d["source"] = "fallback"
+    return d
+
+
+def layer_flops(tokens):
+    routed = 2 * tokens * K * (H * I + I * H)
+    shared = 2 * tokens * (H * IS + IS * H)
+    router = 2 * tokens * H * E
+    return routed, shared, router
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.lines = []
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.th.join(timeout=2)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------- weights
+def make_weights(torch, nk, dev, kind, seed=1234):
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def randn(*shape, std=1.0):
+        return torch.randn(*shape, device=dev, generator=g, dtype=torch.float32).mul_(std)
+
+    router = randn(E, H, std=0.02)
+    w = nk.MoeWeights(hidden=H, experts=E, top_k=K, inter=I, shared_inter=IS,
+                      route_mode=nk.ROUTE_SIGMOID_RENORM,
+                      weight_kind=nk.W_BF16 if kind == "bf16" else nk.W_INT8_ROW,
+                      router_w3=nk.router_split(router))
+    shapes = {"up": (E, I, H), "down": (E, H, I), "shared_up": (IS, H), "shared_down": (H, IS)}
+    for name, shp in shapes.items():
+        f = randn(*shp, std=0.02).to(torch.bfloat16)
+        if kind == "bf16":
+            setattr(w, f"{name}_w", f)
+        else:
+            q, s = nk.quantize_int8_row(f.float().reshape(-1, shp[-1]))
+            setattr(w, f"{name}_w", q.reshape(shp))
+            setattr(w, f"{name}_scale", s)
+            del f
+    host_ref = {"router": router}
+    return w, host_ref
+
+
+# ---------------------------------------------------------------- cpu side
+def cpu_sample(weights_np, x_np, tokens, threads, orc):
+    """Oracle MoE (the reference's algorithm, gathered rows) over `tokens` rows
+    split across `threads` host threads; returns seconds."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    chunks = [c for c in _split(tokens, threads) if c[1] > c[0]]
+
+    def run(c):
+        a, b = c
+        orc.moe(H, E, K, I, IS, weights_np["router_kn"], None, weights_np["up_kn"], None,
+                weights_np["down_kn"], None, weights_np["sup_kn"], None, weights_np["sdown_kn"],
+                None, x_np[a:b], b - a, orc.SIGMOID_RENORM)
+
+    t0 = time.perf_counter()
+    if len(chunks) == 1:
+        run(chunks[0])
+    else:
+        with ThreadPoolExecutor(len(chunks)) as ex:
+            list(ex.map(run, chunks))
+    return time.perf_counter() - t0
+
+
+def _split(n, parts):
+    return [(n * i // parts, n * (i + 1) // parts) for i in range(parts)]
+
+
+def host_weights_from_numpy(seed=1234):
+    """Reference-layout ([in, out]) f32 weights generated on the host."""
+    import numpy as np
+
+    r = np.random.default_rng(seed)
+
+    def randn(*shape):
+        return (r.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+
+    return {"router_kn": randn(H, E), "up_kn": randn(E, H, I), "down_kn": randn(E, I, H),
+            "sup_kn": randn(H, IS), "sdown_kn": randn(IS, H)}
+
+
+def host_weights_from_device(torch, w, router):
+    """The GPU arm's own weights, converted to the reference layout (bf16 weights only)."""
+    def t(x, perm):
+        return x.float().permute(*perm).contiguous().cpu().numpy()
+
+    return {"router_kn": router.t().contiguous().cpu().numpy(),
+            "up_kn": t(w.up_w, (0, 2, 1)), "down_kn": t(w.down_w, (0, 2, 1)),
+            "sup_kn": t(w.shared_up_w, (1, 0)), "sdown_kn": t(w.shared_down_w, (1, 0))}
+
+
+def calibrate_tokens(fn, budget_s, max_tokens):
+    """Token count whose sample takes about budget_s seconds."""
+    t2 = fn(2)
+    per = max(t2 / 2, 1e-4)
+    return max(2, min(max_tokens, int(budget_s / per))), per
+
+
+# ---------------------------------------------------------------- arms
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as orc
+
+    threads = os.cpu_count() or 1
+    wnp = host_weights_from_numpy()
+    x = np.random.default_rng(7).standard_normal((T, H), dtype=np.float32)
+    x = x.astype(np.float32)
+    n_tok, _ = calibrate_tokens(lambda n: cpu_sample(wnp, x, n, min(threads, n), orc), 20.0 /
+                                max(args.steps, 1), T)
+    for _ in range(args.warmup):
+        cpu_sample(wnp, x, min(threads, n_tok), min(threads, n_tok), orc)
+    secs = [cpu_sample(wnp, x, n_tok, min(threads, n_tok), orc) for _ in range(args.steps)]
+    total = sum(secs)
+    value = n_tok * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32/f64-accumulate", "data": "synthetic",
+        "config": config_dict(args, "reference"),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": min(threads, n_tok),
+                         "kind": "port",
+                         "sample": f"{n_tok} of {T} tokens per step, the reference's MoE host "
+                                   "algorithm (oracle/nk_oracle.c, gathered rows) over "
+                                   f"{min(threads, n_tok)} threads"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(args, impl):
+    return {"workload": "MoE layer prefill (BASELINE config 3)", "tokens_per_gpu": T,
+            "hidden": H, "experts": E, "top_k": K, "expert_inter": I, "shared_inter": IS,
+            "routing": "sigmoid top-6 renormalised", "weights": args.weights,
+            "parallelism": f"replicas x{args.gpus} (expert-parallel dispatch not yet built)",
+            "l2": "256 MiB buffer written between timed steps",
+            "impl": impl}
+
+
+def nk_arm(args):
+    import numpy as np
+    import torch
+
+    import nk
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+    nk.lib()
+
+    w, ref = make_weights(torch, nk, dev, args.weights)
+    layer = nk.MoeLayer(w)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(T, H, device=dev, dtype=torch.float32)
+    idx = torch.empty(T * K, device=dev, dtype=torch.int32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        layer.forward(x, out=out, indices=idx)
+    nk.device_status()
+    barrier()
+
+    sampler = ClockSampler(local)
+    time.sleep(0.2)
+    nk.set_stage_timing(True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stage_sum = {}
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        layer.forward(x, out=out, indices=idx)
+        ends[i].record(stream)
+        for kname, v in nk.moe_stage_times().items():
+            stage_sum[kname] = stage_sum.get(kname, 0.0) + v
+    barrier()
+    nk.set_stage_timing(False)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+    # e2e: host (pinned) input -> device -> forward -> host output, every step
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    xin = torch.empty_like(x)
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        e_starts[i].record(stream)
+        xin.copy_(x_host, non_blocking=True)
+        layer.forward(xin, out=out, indices=idx)
+        out_host.copy_(out, non_blocking=True)
+        e_ends[i].record(stream)
+    barrier()
+    clocks = sampler.stop()
+    nk.device_status()
+    e2e_ms = [s.elapsed_time(e) for s, e in zip(e_starts, e_ends)]
+
+    total_ms = sum(step_ms)
+    total_e2e = sum(e2e_ms)
+    up_ms = stage_sum.get("up_proj", 0.0) / args.steps
+    down_ms = stage_sum.get("down_proj", 0.0) / args.steps
+    if world > 1:
+        t = torch.tensor([total_ms, total_e2e, up_ms + down_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms, total_e2e, _ = t.tolist()
+
+    if rank == 0:
+        pk = peaks()
+        counts = np.bincount(idx.cpu().numpy(), minlength=E)
+        active = int((counts > 0).sum())
+        wbytes_per = 1 if args.weights == "int8" else 2
+        expert_w_bytes = active * 2 * I * H * wbytes_per
+        slots = T * K
+        act_bytes = slots * H * 2 + 2 * slots * I * 2 + slots * H * 2
+        grouped_bytes = expert_w_bytes + act_bytes
+        grouped_ms = up_ms + down_ms
+        routed, shared, router = layer_flops(T)
+        tokens_total = T * world * args.steps
+        value = tokens_total / (total_ms / 1e3)
+        ach_gbs = grouped_bytes / (grouped_ms / 1e3) / 1e9
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                traffic = json.load(f).get(f"moe_grouped_{args.weights}")
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.weights == "bf16" else "bf16 activations, int8 weights",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": config_dict(args, "nk"),
+            "tflops": (routed + shared + router) * world * args.steps / (total_ms / 1e3) / 1e12,
+            "tensor_frac_of_measured": ((routed + shared + router) / (total_ms / args.steps / 1e3)
+                                        / 1e12) / pk["bf16_tflops"],
+            "stages_ms": {k2: v / args.steps for k2, v in stage_sum.items()},
+            "roofline": {
+                "kernel": "tc_gemm_kernel grouped up + down projections (2 launches per step)",
+                "bound": "hbm", "achieved": ach_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": ach_gbs / pk["hbm_gbs"], "traffic": traffic,
+                "peak_source": pk["source"],
+                "algorithmic_bytes_per_step": grouped_bytes,
+                "tensor_tflops": routed / (grouped_ms / 1e3) / 1e12,
+                "tensor_frac": routed / (grouped_ms / 1e3) / 1e12 / pk["bf16_tflops"],
+            },
+            "e2e": {"value": tokens_total / (total_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
+            "clocks": clocks,
+            "gpu_launches": 13 * args.steps * 2,
+        }
+        if world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle as orc
+
+            wnp = host_weights_from_device(torch, w, ref["router"])
+            xs = x[:64].float().cpu().numpy()
+            n_tok, _ = calibrate_tokens(lambda n: cpu_sample(wnp, xs, n, 1, orc), 15.0, 64)
+            secs = cpu_sample(wnp, xs, n_tok, 1, orc)
+            line["cpu_baseline"] = {
+                "value": n_tok / secs, "unit": "tokens/s", "cores": 1, "kind": "port",
+                "sample": f"{n_tok} of {T} tokens: oracle/nk_oracle.c restatement of "
+                          "MoeLayer::forward_into (f64-accumulate GEMM loops) on the GPU arm's "
+                          "weights, single thread, gathered rows (the reference itself runs "
+                          "every selected expert over all rows)"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["nk", "reference"], default="nk")
+    ap.add_argument("--weights", choices=["bf16", "int8"], default="bf16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=T,
+                    help="tokens per GPU (profiling captures use a smaller case)")
+    ap.add_argument("--experts", type=int, default=E)
+    args = ap.parse_args()
+    globals()["T"], globals()["E"] = args.tokens, args.experts
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return reference_arm(args)
+    return nk_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -249,6 +249,19 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
                          void *out, int32_t out_dtype, int32_t *indices, float *weights,
                          void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---------------------------------------------------------------- tracing */
+
+/* Stage timing of nk_moe_forward (not in the reference, whose only timing is
+ * wall-clock around whole calls, nemotron-validate/src/benchmark.rs:465-500).
+ * While enabled on the calling thread, nk_moe_forward records CUDA events on
+ * its stream between stages; nk_moe_stage_times waits for the last call's
+ * final event and returns the milliseconds of each stage:
+ *   0 router GEMM, 1 routing + plan + tile lists, 2 token gather,
+ *   3 grouped up-projection, 4 grouped down-projection, 5 shared expert,
+ *   6 combine. */
+nk_status nk_set_stage_timing(int32_t enable);
+nk_status nk_moe_stage_times(float *ms, int32_t capacity, int32_t *count);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

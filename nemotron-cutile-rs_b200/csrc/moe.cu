@@ -87,6 +87,23 @@ __global__ void combine_kernel(const __nv_bfloat16 *__restrict__ y,
 
 namespace {
 
+constexpr int kStages = 7;
+struct StageTimer {
+  bool enabled = false;
+  bool recorded = false;
+  cudaEvent_t ev[kStages + 1] = {};
+  void mark(int i, cudaStream_t s) {
+    if (!enabled) return;
+    if (!ev[i]) cudaEventCreate(&ev[i]);
+    cudaEventRecord(ev[i], s);
+    if (i == kStages) recorded = true;
+  }
+};
+StageTimer &timer() {
+  static thread_local StageTimer t;
+  return t;
+}
+
 struct MoeWorkspace {
   float *scores;
   int32_t *idx;
@@ -208,6 +225,9 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
   float *rw = weights ? weights : ws.w;
   nk_status st;
 
+  StageTimer &tm = timer();
+  tm.recorded = false;
+  tm.mark(0, s);
   // 1. router scores [T, E] f32: x · (hi + mid + lo)ᵀ, bias after.
   {
     const int64_t hp = ceil_div(H, 64) * 64;
@@ -228,6 +248,7 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
     st = tc_gemm(WK_BF16, L.router_w3, E, 3 * hp, 3 * hp * 2, x, T, H, H, bn, a, grid, s);
     if (st != NK_OK) return st;
   }
+  tm.mark(1, s);
   // 2. routing, 3. plan
   st = launch_route(ws.scores, T, (int)E, (int)K, L.route_mode, idx, rw, s);
   if (st != NK_OK) return st;
@@ -239,6 +260,7 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
                                         ws.tiles_down, ws.tile_counts + 1);
   st = check_launch("build_tiles_kernel");
   if (st != NK_OK) return st;
+  tm.mark(2, s);
   // 4. gather routed token rows in expert order
   {
     const int warps = 8;
@@ -248,6 +270,7 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
     st = check_launch("gather_rows_kernel");
     if (st != NK_OK) return st;
   }
+  tm.mark(3, s);
   // 5. grouped up-projection + relu2: hmid[pos, :] = relu2(xp[pos] · up_eᵀ + b)
   {
     TcArgs a = base_args(err);
@@ -263,6 +286,7 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
                  num_sms(), s);
     if (st != NK_OK) return st;
   }
+  tm.mark(4, s);
   // 6. grouped down-projection: y[pos, :] = hmid[pos] · down_eᵀ + b  (into xp's storage)
   uint16_t *yrouted = ws.xp;
   {
@@ -278,6 +302,7 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
                  num_sms(), s);
     if (st != NK_OK) return st;
   }
+  tm.mark(5, s);
   // 7. shared expert over all tokens
   if (L.shared_inter > 0) {
     const int64_t Is = L.shared_inter;
@@ -288,6 +313,7 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
                L.shared_down_b, ws.s1, T, Is, H, ws.sh, false, false, err, s);
     if (st != NK_OK) return st;
   }
+  tm.mark(6, s);
   // 8. combine in rank order
   if (out_dtype == NK_F32)
     combine_kernel<true><<<(unsigned)T, 256, 0, s>>>(
@@ -297,7 +323,9 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
     combine_kernel<false><<<(unsigned)T, 256, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16 *>(yrouted),
         reinterpret_cast<const __nv_bfloat16 *>(ws.sh), rw, ws.slot_pos, H, (int)K, out);
-  return check_launch("combine_kernel");
+  st = check_launch("combine_kernel");
+  tm.mark(7, s);
+  return st;
 }
 
 }  // namespace nk
@@ -325,6 +353,21 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
   st = moe_forward(*layer, x, tokens, out, out_dtype, indices, weights, workspace,
                    workspace_bytes, as_stream(stream));
   return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_set_stage_timing(int32_t enable) {
+  timer().enabled = enable != 0;
+  return ok();
+}
+
+nk_status nk_moe_stage_times(float *ms, int32_t capacity, int32_t *count) {
+  StageTimer &t = timer();
+  if (!t.recorded) return fail(NK_INVALID_PARAMS, "no timed nk_moe_forward on this thread");
+  NK_CUDA_TRY(cudaEventSynchronize(t.ev[kStages]));
+  int n = capacity < kStages ? capacity : kStages;
+  for (int i = 0; i < n; ++i) NK_CUDA_TRY(cudaEventElapsedTime(&ms[i], t.ev[i], t.ev[i + 1]));
+  if (count) *count = n;
+  return ok();
 }
 
 }  // extern "C"

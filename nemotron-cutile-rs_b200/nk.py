@@ -102,7 +102,23 @@ _SIGS = {
     "nk_linear_pack_kn": (_i32, [_p, _i64, _i64, _p, _p]),
     "nk_moe_workspace_bytes": (_i32, [_p, _i64, _p]),
     "nk_moe_forward": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+    "nk_set_stage_timing": (_i32, [_i32]),
+    "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }
+MOE_STAGES = ("router", "route_plan", "gather", "up_proj", "down_proj", "shared_expert",
+              "combine")
+
+
+def set_stage_timing(enable: bool) -> None:
+    call("nk_set_stage_timing", 1 if enable else 0)
+
+
+def moe_stage_times() -> dict:
+    """Per-stage milliseconds of this thread's last nk_moe_forward (see nk.h)."""
+    arr = (ctypes.c_float * len(MOE_STAGES))()
+    n = ctypes.c_int32(0)
+    call("nk_moe_stage_times", arr, len(MOE_STAGES), ctypes.byref(n))
+    return {MOE_STAGES[i]: float(arr[i]) for i in range(n.value)}
 
 _lib = None
 
@@ -155,11 +171,6 @@ def _require_cuda(*tensors):
     for t in tensors:
         if t is not None and not t.is_cuda:
             raise RuntimeError("libnk entry points take device tensors")
-
-
-def bf16_bits(t):
-    """View a bf16 tensor's storage for the uint16_t* parameters."""
-    return t
 
 
 # ------------------------------------------------------------ kernel wrappers
@@ -220,7 +231,7 @@ def moe_route(scores, tokens: int, experts: int, top_k: int, mode: int = ROUTE_S
 
     _require_cuda(scores)
     dev = scores.device
-    n = max(tokens * top_k, 1)
+    n = max(tokens * top_k, 1)  # placeholder storage when the batch is empty
     idx = torch.empty(n, dtype=torch.int32, device=dev)
     w = torch.empty(n, dtype=torch.float32, device=dev)
     call("nk_moe_route", ptr(scores), scores.numel(), tokens, experts, top_k, mode, ptr(idx),
