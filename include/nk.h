@@ -125,6 +125,22 @@ nk_status nk_gemm_w4a(const void *x, int32_t x_dtype, const uint8_t *packed, siz
                       int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
                       void *stream);
 
+/* Allocation-free variant of nk_gemm_w8row for f32 activations.  It has no
+ * counterpart in the reference.  For callers that cannot let a library call
+ * cudaMalloc (a host whose device memory belongs to its own pool, or a
+ * latency-critical path where an allocation would synchronise the device):
+ * the exact bf16 split of x lives in a fixed 8 MiB device array inside
+ * libnk, held by every GPU that loads the library until exit, instead of the
+ * library's growable scratch.  m * 4 * ceil(k/64)*64 bytes must fit in 8 MiB
+ * (NK_WORKSPACE_TOO_SMALL otherwise); k % 16 == 0.  All calls on a device
+ * share the array, so calls that overlap on the GPU race; each call rewrites
+ * all of it that it reads.  The first call on a device resolves the array's
+ * device address and should come before any stream capture.  Same output
+ * contract as nk_gemm_w8row(x_dtype = NK_F32). */
+nk_status nk_gemm_w8row_f32_static(const float *x, const int8_t *wq, const float *scales,
+                                   const float *bias, void *y, int32_t y_dtype, int64_t m,
+                                   int64_t k, int64_t n, int32_t flags, void *stream);
+
 /* -------------------------------------------------------------- quantize */
 
 /* quantize.rs:59-81 pack_int4_into_host.  Synchronises `stream` (the range

@@ -89,6 +89,7 @@ _SIGS = {
     "nk_gemm_f32": (_i32, [_p, _sz, _p, _sz, _p, _sz, _sz, _sz, _sz, _p]),
     "nk_gemm_bf16": (_i32, [_p, _i32, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
     "nk_gemm_w8row": (_i32, [_p, _i32, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
+    "nk_gemm_w8row_f32_static": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
     "nk_gemm_w4a": (_i32, [_p, _i32, _p, _sz, _f, _u32, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
     "nk_pack_int4": (_i32, [_p, _sz, _p, _sz, _p]),
     "nk_unpack_int4": (_i32, [_p, _sz, _sz, _p, _sz, _p]),
