@@ -230,6 +230,8 @@ def config_dict(args, impl):
             "routing": "sigmoid top-6 renormalised", "weights": args.weights,
             "parallelism": f"replicas x{args.gpus} (expert-parallel dispatch not yet built)",
             "l2": "256 MiB buffer written between timed steps",
+            "launch": "CUDA graph of the nk_moe_forward call" if args.graph
+                      else "eager launches",
             "impl": impl}
 
 
@@ -266,14 +268,27 @@ def nk_arm(args):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    nk.set_stage_timing(True)  # events are created during warm-up, before any capture
     for _ in range(args.warmup):
         layer.forward(x, out=out, indices=idx)
     nk.device_status()
     barrier()
 
+    # With --graph the step replays a CUDA graph captured from the C-ABI call
+    # (the 14 kernel launches of one forward), stage-timing events included.
+    xin = torch.empty_like(x)
+    fwd = lambda: layer.forward(x, out=out, indices=idx)  # noqa: E731
+    fwd_e2e = lambda: layer.forward(xin, out=out, indices=idx)  # noqa: E731
+    if args.graph:
+        graphs = []
+        for fn in (fwd, fwd_e2e):
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_):
+                fn()
+            graphs.append(g_)
+        fwd, fwd_e2e = graphs[0].replay, graphs[1].replay
     sampler = ClockSampler(local)
     time.sleep(0.2)
-    nk.set_stage_timing(True)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     stage_sum = {}
@@ -281,7 +296,7 @@ def nk_arm(args):
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
-        layer.forward(x, out=out, indices=idx)
+        fwd()
         ends[i].record(stream)
         for kname, v in nk.moe_stage_times().items():
             stage_sum[kname] = stage_sum.get(kname, 0.0) + v
@@ -292,13 +307,12 @@ def nk_arm(args):
     # e2e: host (pinned) input -> device -> forward -> host output, every step
     e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    xin = torch.empty_like(x)
     barrier()
     for i in range(args.steps):
         flush.zero_()
         e_starts[i].record(stream)
         xin.copy_(x_host, non_blocking=True)
-        layer.forward(xin, out=out, indices=idx)
+        fwd_e2e()
         out_host.copy_(out, non_blocking=True)
         e_ends[i].record(stream)
     barrier()
@@ -328,7 +342,7 @@ def nk_arm(args):
         routed, shared, router = layer_flops(T)
         tokens_total = T * world * args.steps
         value = tokens_total / (total_ms / 1e3)
-        ach_gbs = grouped_bytes / (grouped_ms / 1e3) / 1e9
+        ach_gbs = grouped_bytes / (grouped_ms / 1e3) / 1e9 if grouped_ms > 0 else float("nan")
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
@@ -357,7 +371,7 @@ def nk_arm(args):
             "e2e": {"value": tokens_total / (total_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
             "clocks": clocks,
-            "gpu_launches": 13 * args.steps * 2,
+            "gpu_launches": 14 * args.steps * 2,
         }
         if world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
             sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -390,6 +404,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=T,
                     help="tokens per GPU (profiling captures use a smaller case)")
     ap.add_argument("--experts", type=int, default=E)
+    ap.add_argument("--graph", action="store_true",
+                    help="replay the forward as a captured CUDA graph (measured no faster "
+                         "than eager launches: the step is device-bound)")
     args = ap.parse_args()
     globals()["T"], globals()["E"] = args.tokens, args.experts
     if args.warmup < 3:

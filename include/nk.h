@@ -274,7 +274,9 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
  * final event and returns the milliseconds of each stage:
  *   0 router GEMM, 1 routing + plan + tile lists, 2 token gather,
  *   3 grouped up-projection, 4 grouped down-projection, 5 shared expert,
- *   6 combine. */
+ *   6 combine.
+ * A forward captured into a CUDA graph while timing is enabled records its
+ * events as graph nodes; after each replay nk_moe_stage_times reads them. */
 nk_status nk_set_stage_timing(int32_t enable);
 nk_status nk_moe_stage_times(float *ms, int32_t capacity, int32_t *count);
 

@@ -8,11 +8,25 @@
 
 namespace nk {
 
+// Tile t of the launch.  With k_splits > 1 (dense grids only) consecutive tile
+// indices are the K splits of one output tile; every split covers >= 1 K block.
 template <int BN>
-__device__ __forceinline__ bool load_tile(const TcArgs &a, int t, TcTile &tile) {
+__device__ __forceinline__ bool load_tile(const TcArgs &a, int t, TcTile &tile, int &k_begin,
+                                          int &k_count, int &split) {
+  k_begin = 0;
+  k_count = a.k_blocks;
+  split = 0;
   if (a.tiles) {
     tile = a.tiles[t];
     return true;
+  }
+  if (a.k_splits > 1) {
+    const int per = (a.k_blocks + a.k_splits - 1) / a.k_splits;
+    split = t % a.k_splits;
+    t /= a.k_splits;
+    k_begin = split * per;
+    const int left = a.k_blocks - k_begin;
+    k_count = left < per ? left : per;
   }
   int ft = t / a.t_tiles, tt = t - ft * a.t_tiles;
   tile.w_row = ft * 128;
@@ -75,7 +89,9 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = args.tiles ? *args.tile_count : args.f_tiles * args.t_tiles;
+  const int num_tiles = args.tiles ? *args.tile_count
+                                   : args.f_tiles * args.t_tiles *
+                                         (args.k_splits > 1 ? args.k_splits : 1);
   volatile int *abort_v = &abort_flag;
 
   if (warp == 0) {
@@ -87,12 +103,14 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         TcTile tile;
-        load_tile<BN>(args, t, tile);
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        int k_begin, k_count, split;
+        load_tile<BN>(args, t, tile, k_begin, k_count, split);
+        for (int kk = 0; kk < k_count; ++kk) {
           if (*abort_v || !mbar_wait(&empty[stage], phase ^ 1, err)) {
             ok = false;
             break;
           }
+          const int kb = k_begin + kk;
           int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
           int xkb = args.x_k_period > 0 ? kb % args.x_k_period : kb;
           mbar_arrive_expect_tx(&full[stage], (WK == WK_BF16 ? Cfg::kABytes : Cfg::kRawBytes) +
@@ -131,7 +149,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
       const uint32_t a_base = smem_u32(a_tiles), b_base = smem_u32(b_tiles);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         TcTile tile;
-        load_tile<BN>(args, t, tile);
+        int k_begin, k_count, split;
+        load_tile<BN>(args, t, tile, k_begin, k_count, split);
         int t_valid = tile.valid & 0xFFFF;
         uint32_t n_mma = (uint32_t)((t_valid + 15) & ~15);
         if (n_mma < 16) n_mma = 16;
@@ -143,7 +162,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = 0; kb < k_count; ++kb) {
           bool got = WK == WK_BF16 ? mbar_wait(&full[stage], phase, err)
                                    : mbar_wait(&conv[stage], phase, err);
           if (*abort_v || !got) {
@@ -182,7 +201,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       TcTile tile;
-      load_tile<BN>(args, t, tile);
+      int k_begin, k_count, split;
+      load_tile<BN>(args, t, tile, k_begin, k_count, split);
       const int f_valid = tile.valid >> 16, t_valid = tile.valid & 0xFFFF;
       // warp-uniform decision: tcgen05.ld below is .sync.aligned
       const bool stop = __any_sync(0xffffffffu, *abort_v || !mbar_wait(&tfull[acc], acc_phase, err));
@@ -212,7 +232,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
               if (args.relu2) o = nk_relu2(o);
               if (args.tok_scale) o *= args.tok_scale[tile.x_row + j];
               const long long off =
-                  (long long)(tile.x_row + j) * args.ldy + tile.out_col0 + i;
+                  (long long)(tile.x_row + j) * args.ldy + tile.out_col0 + i +
+                  split * args.split_stride;
               if (args.y_f32)
                 reinterpret_cast<float *>(args.y)[off] = o;
               else
@@ -235,7 +256,10 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       bool ok = true;
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
+      TcTile tile;
+      int k_begin, k_count, split;
+      load_tile<BN>(args, t, tile, k_begin, k_count, split);
+      for (int kb = 0; kb < k_count; ++kb) {
         if (*abort_v || !mbar_wait(&full[stage], phase, err)) {
           ok = false;
           break;

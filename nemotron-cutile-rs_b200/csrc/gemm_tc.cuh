@@ -46,6 +46,8 @@ struct TcArgs {
   int k_blocks;             // 64-wide K blocks of the contraction
   int w_k_period;           // >0: weight K block = kb % w_k_period
   int x_k_period;           // >0: activation K block = kb % x_k_period
+  int k_splits;             // dense only: >1 splits K over tiles; split s writes its
+  long long split_stride;   //   partial sums at y + s * split_stride (elements)
   // epilogue
   void *y;
   long long ldy;

@@ -10,6 +10,7 @@
 namespace nk {
 
 constexpr int kMoeBN = 256;
+constexpr int kRouterMaxSplits = 16;
 
 // Grouped tile list: for each expert e with c_e routed rows, ceil(n_out/128)
 // feature tiles x ceil(c_e/BN) token tiles.  One block; E <= 1024.
@@ -59,12 +60,23 @@ __global__ void gather_rows_kernel(const uint4 *__restrict__ x, const int32_t *_
 }
 
 // out[t, c] = 0 (+ shared[t, c]) + Σ_r w[t, r] * y[slot_pos[t*k + r], c], each
-// product and sum rounded in f32 in rank order (moe.rs:195-246).
+// product and sum rounded in f32 in rank order (moe.rs:195-246).  One block per
+// token; each thread owns 8 consecutive columns (16-byte loads; H % 8 == 0).
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 &v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
 template <bool OUT_F32>
-__global__ void combine_kernel(const __nv_bfloat16 *__restrict__ y,
-                               const __nv_bfloat16 *__restrict__ shared,
-                               const float *__restrict__ w, const int32_t *__restrict__ slot_pos,
-                               int64_t H, int top_k, void *__restrict__ out) {
+__global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16 *__restrict__ y,
+                                                      const __nv_bfloat16 *__restrict__ shared,
+                                                      const float *__restrict__ w,
+                                                      const int32_t *__restrict__ slot_pos,
+                                                      int64_t H, int top_k, void *__restrict__ out) {
   const int64_t t = blockIdx.x;
   __shared__ int32_t pos[32];
   __shared__ float wt[32];
@@ -73,16 +85,50 @@ __global__ void combine_kernel(const __nv_bfloat16 *__restrict__ y,
     wt[threadIdx.x] = w[t * top_k + threadIdx.x];
   }
   __syncthreads();
-  for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
-    float o = 0.0f;
-    if (shared) o = __fadd_rn(o, __bfloat162float(shared[t * H + c]));
-    for (int r = 0; r < top_k; ++r)
-      o = __fadd_rn(o, __fmul_rn(wt[r], __bfloat162float(y[(int64_t)pos[r] * H + c])));
-    if (OUT_F32)
-      reinterpret_cast<float *>(out)[t * H + c] = o;
-    else
-      reinterpret_cast<__nv_bfloat16 *>(out)[t * H + c] = __float2bfloat16_rn(o);
+  const int64_t vecs = H >> 3;
+  for (int64_t v = threadIdx.x; v < vecs; v += blockDim.x) {
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+    if (shared) {
+      float sf[8];
+      bf16x8_to_f32(reinterpret_cast<const uint4 *>(shared + t * H)[v], sf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(o[i], sf[i]);
+    }
+    for (int r = 0; r < top_k; ++r) {
+      float yf[8];
+      bf16x8_to_f32(reinterpret_cast<const uint4 *>(y + (int64_t)pos[r] * H)[v], yf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(o[i], __fmul_rn(wt[r], yf[i]));
+    }
+    if (OUT_F32) {
+      float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + t * H) + 2 * v;
+      dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+        pk[i] = *reinterpret_cast<uint32_t *>(&b);
+      }
+      reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(out) + t * H)[v] =
+          make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
   }
+}
+
+// scores[i] = (Σ_s partial[s][i]) + bias[i % E], partial sums added in split order.
+__global__ void router_reduce_kernel(const float *__restrict__ partial, int splits, int64_t n,
+                                     int E, const float *__restrict__ bias,
+                                     float *__restrict__ scores) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = partial[i];
+  for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, partial[(int64_t)s * n + i]);
+  if (bias) acc = __fadd_rn(acc, bias[i % E]);
+  scores[i] = acc;
 }
 
 namespace {
@@ -95,7 +141,14 @@ struct StageTimer {
   void mark(int i, cudaStream_t s) {
     if (!enabled) return;
     if (!ev[i]) cudaEventCreate(&ev[i]);
-    cudaEventRecord(ev[i], s);
+    // Inside a stream capture the record becomes a graph node; "external" makes
+    // the event observable after each replay of the graph.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+      cudaEventRecordWithFlags(ev[i], s, cudaEventRecordExternal);
+    else
+      cudaEventRecord(ev[i], s);
     if (i == kStages) recorded = true;
   }
 };
@@ -106,6 +159,7 @@ StageTimer &timer() {
 
 struct MoeWorkspace {
   float *scores;
+  float *router_partial;  // [splits, T, E]
   int32_t *idx;
   float *w;
   int32_t *counts, *offsets, *perm, *slot_pos, *plan_scratch;
@@ -130,6 +184,7 @@ MoeWorkspace carve(const nk_moe_layer &L, int64_t T, uint8_t *base) {
   };
   const int64_t E = L.experts, K = L.top_k, H = L.hidden, I = L.inter, S = T * K;
   ws.scores = (float *)take(sizeof(float) * T * E);
+  ws.router_partial = (float *)take(sizeof(float) * T * E * kRouterMaxSplits);
   ws.idx = (int32_t *)take(sizeof(int32_t) * S);
   ws.w = (float *)take(sizeof(float) * S);
   ws.counts = (int32_t *)take(sizeof(int32_t) * E);
@@ -228,24 +283,40 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
   StageTimer &tm = timer();
   tm.recorded = false;
   tm.mark(0, s);
-  // 1. router scores [T, E] f32: x · (hi + mid + lo)ᵀ, bias after.
+  // 1. router scores [T, E] f32: x · (hi + mid + lo)ᵀ.  K is split over CTAs into
+  //    f32 partial sums, reduced in split order; the bias is added after the
+  //    GEMM as linear.rs:333-339 does.
   {
     const int64_t hp = ceil_div(H, 64) * 64;
     const int bn = T <= 64 ? 64 : 256;
+    const int k_blocks = (int)(3 * hp / 64);
     TcArgs a = base_args(err);
     a.f_tiles = (int)ceil_div(E, 128);
     a.t_tiles = (int)ceil_div(T, bn);
+    const int base_tiles = a.f_tiles * a.t_tiles;
+    int want = num_sms() / base_tiles;
+    if (want < 1) want = 1;
+    if (want > kRouterMaxSplits) want = kRouterMaxSplits;
+    if (want > k_blocks) want = k_blocks;
+    const int per = (int)ceil_div(k_blocks, want);
+    const int splits = (int)ceil_div(k_blocks, per);  // every split gets >= 1 block
     a.n_features = (int)E;
     a.n_tokens = (int)T;
-    a.k_blocks = (int)(3 * hp / 64);
+    a.k_blocks = k_blocks;
     a.x_k_period = (int)(hp / 64);
-    a.y = ws.scores;
+    a.k_splits = splits;
+    a.split_stride = T * E;
+    a.y = ws.router_partial;
     a.ldy = E;
     a.y_f32 = 1;
-    a.bias = L.router_b;
-    int64_t tiles = (int64_t)a.f_tiles * a.t_tiles;
+    int64_t tiles = (int64_t)base_tiles * splits;
     int grid = (int)(tiles < num_sms() ? tiles : num_sms());
     st = tc_gemm(WK_BF16, L.router_w3, E, 3 * hp, 3 * hp * 2, x, T, H, H, bn, a, grid, s);
+    if (st != NK_OK) return st;
+    const int64_t n = T * E;
+    router_reduce_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
+        ws.router_partial, splits, n, (int)E, L.router_b, ws.scores);
+    st = check_launch("router_reduce_kernel");
     if (st != NK_OK) return st;
   }
   tm.mark(1, s);
@@ -316,11 +387,11 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
   tm.mark(6, s);
   // 8. combine in rank order
   if (out_dtype == NK_F32)
-    combine_kernel<true><<<(unsigned)T, 256, 0, s>>>(
+    combine_kernel<true><<<(unsigned)T, 128, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16 *>(yrouted),
         reinterpret_cast<const __nv_bfloat16 *>(ws.sh), rw, ws.slot_pos, H, (int)K, out);
   else
-    combine_kernel<false><<<(unsigned)T, 256, 0, s>>>(
+    combine_kernel<false><<<(unsigned)T, 128, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16 *>(yrouted),
         reinterpret_cast<const __nv_bfloat16 *>(ws.sh), rw, ws.slot_pos, H, (int)K, out);
   st = check_launch("combine_kernel");
