@@ -186,6 +186,48 @@ def calibrate_tokens(fn, budget_s, max_tokens):
     return max(2, min(max_tokens, int(budget_s / per))), per
 
 
+class EpTimer:
+    """Wraps nk_ep.NkBackend and times its stages with CUDA events on the
+    current stream (dispatch, grouped experts, shared + combine); the rest of
+    a step is the NCCL exchange."""
+
+    def __init__(self, be, torch):
+        self.be, self.torch = be, torch
+        self.ev = []
+
+    def _mark(self, name):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.ev.append((name, e))
+
+    def dispatch(self, x):
+        self.ev = []
+        self._mark("start")
+        r = self.be.dispatch(x)
+        self._mark("dispatch")
+        return r
+
+    def experts(self, rows, seg_expert, seg_rows):
+        self._mark("exchange_in")
+        r = self.be.experts(rows, seg_expert, seg_rows)
+        self._mark("experts")
+        return r
+
+    def shared(self, x):
+        self._mark("exchange_out")
+        return self.be.shared(x)
+
+    def combine(self, *a):
+        r = self.be.combine(*a)
+        self._mark("shared_combine")
+        return r
+
+    def step_times(self):
+        self.ev[-1][1].synchronize()
+        return {self.ev[i][0]: self.ev[i - 1][1].elapsed_time(self.ev[i][1])
+                for i in range(1, len(self.ev))}
+
+
 # ---------------------------------------------------------------- arms
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -228,7 +270,9 @@ def config_dict(args, impl):
     return {"workload": "MoE layer prefill (BASELINE config 3)", "tokens_per_gpu": T,
             "hidden": H, "experts": E, "top_k": K, "expert_inter": I, "shared_inter": IS,
             "routing": "sigmoid top-6 renormalised", "weights": args.weights,
-            "parallelism": f"replicas x{args.gpus} (expert-parallel dispatch not yet built)",
+            "parallelism": (f"expert-parallel x{args.gpus}: {E // max(args.gpus, 1)} experts per "
+                            "rank, NCCL all-to-all-v of routed rows" if args.gpus > 1
+                            else "single GPU, all experts"),
             "l2": "256 MiB buffer written between timed steps",
             "launch": "CUDA graph of the nk_moe_forward call" if args.graph
                       else "eager launches",
@@ -253,7 +297,6 @@ def nk_arm(args):
     nk.lib()
 
     w, ref = make_weights(torch, nk, dev, args.weights)
-    layer = nk.MoeLayer(w)
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
     out = torch.empty(T, H, device=dev, dtype=torch.float32)
@@ -262,24 +305,48 @@ def nk_arm(args):
     x_host = x.cpu().pin_memory()
     out_host = torch.empty(T, H, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream()
+    xin = torch.empty_like(x)
+    ep_timer = None
+    if world == 1:
+        layer = nk.MoeLayer(w)
+        fwd = lambda: layer.forward(x, out=out, indices=idx)  # noqa: E731
+        fwd_e2e = lambda: layer.forward(xin, out=out, indices=idx)  # noqa: E731
+    else:
+        from nk_ep import ExpertParallelMoe, NkBackend, local_expert_slice
+
+        el = E // world
+        lw = nk.MoeWeights(hidden=H, experts=el, top_k=1, inter=I, shared_inter=0,
+                           route_mode=w.route_mode, weight_kind=w.weight_kind,
+                           router_w3=w.router_w3,
+                           up_w=local_expert_slice(w.up_w, rank, world, E),
+                           down_w=local_expert_slice(w.down_w, rank, world, E),
+                           up_scale=None if w.up_scale is None else
+                           w.up_scale.reshape(E, I)[rank * el:(rank + 1) * el].reshape(-1),
+                           down_scale=None if w.down_scale is None else
+                           w.down_scale.reshape(E, H)[rank * el:(rank + 1) * el].reshape(-1))
+        ep_timer = EpTimer(NkBackend(w, lw), torch)
+        ep = ExpertParallelMoe(ep_timer, E, H, K)
+
+        def fwd():
+            out.copy_(ep.forward(x)[0])
+
+        def fwd_e2e():
+            out.copy_(ep.forward(xin)[0])
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    nk.set_stage_timing(True)  # events are created during warm-up, before any capture
+    nk.set_stage_timing(world == 1)  # events are created during warm-up, before any capture
     for _ in range(args.warmup):
-        layer.forward(x, out=out, indices=idx)
+        fwd()
     nk.device_status()
     barrier()
 
     # With --graph the step replays a CUDA graph captured from the C-ABI call
     # (the 14 kernel launches of one forward), stage-timing events included.
-    xin = torch.empty_like(x)
-    fwd = lambda: layer.forward(x, out=out, indices=idx)  # noqa: E731
-    fwd_e2e = lambda: layer.forward(xin, out=out, indices=idx)  # noqa: E731
-    if args.graph:
+    if args.graph and world == 1:
         graphs = []
         for fn in (fwd, fwd_e2e):
             g_ = torch.cuda.CUDAGraph()
@@ -298,10 +365,11 @@ def nk_arm(args):
         starts[i].record(stream)
         fwd()
         ends[i].record(stream)
-        for kname, v in nk.moe_stage_times().items():
+        times = nk.moe_stage_times() if world == 1 else ep_timer.step_times()
+        for kname, v in times.items():
             stage_sum[kname] = stage_sum.get(kname, 0.0) + v
     barrier()
-    nk.set_stage_timing(False)
+
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
     # e2e: host (pinned) input -> device -> forward -> host output, every step
@@ -322,23 +390,28 @@ def nk_arm(args):
 
     total_ms = sum(step_ms)
     total_e2e = sum(e2e_ms)
-    up_ms = stage_sum.get("up_proj", 0.0) / args.steps
-    down_ms = stage_sum.get("down_proj", 0.0) / args.steps
+    if world == 1:
+        grouped_ms = (stage_sum.get("up_proj", 0.0) + stage_sum.get("down_proj", 0.0)) / args.steps
+    else:
+        grouped_ms = stage_sum.get("experts", 0.0) / args.steps
     if world > 1:
-        t = torch.tensor([total_ms, total_e2e, up_ms + down_ms], device=dev)
+        t = torch.tensor([total_ms, total_e2e, grouped_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms, total_e2e, _ = t.tolist()
 
     if rank == 0:
         pk = peaks()
-        counts = np.bincount(idx.cpu().numpy(), minlength=E)
-        active = int((counts > 0).sum())
         wbytes_per = 1 if args.weights == "int8" else 2
+        if world == 1:
+            counts = np.bincount(idx.cpu().numpy(), minlength=E)
+            active = int((counts > 0).sum())
+            rows = T * K
+        else:  # this rank's experts and the rows it received in the last step
+            active = E // world
+            rows = int(sum(ep.last_exchange["received_rows"]))
         expert_w_bytes = active * 2 * I * H * wbytes_per
-        slots = T * K
-        act_bytes = slots * H * 2 + 2 * slots * I * 2 + slots * H * 2
+        act_bytes = rows * H * 2 + 2 * rows * I * 2 + rows * H * 2
         grouped_bytes = expert_w_bytes + act_bytes
-        grouped_ms = up_ms + down_ms
         routed, shared, router = layer_flops(T)
         tokens_total = T * world * args.steps
         value = tokens_total / (total_ms / 1e3)
@@ -365,8 +438,8 @@ def nk_arm(args):
                 "frac": ach_gbs / pk["hbm_gbs"], "traffic": traffic,
                 "peak_source": pk["source"],
                 "algorithmic_bytes_per_step": grouped_bytes,
-                "tensor_tflops": routed / (grouped_ms / 1e3) / 1e12,
-                "tensor_frac": routed / (grouped_ms / 1e3) / 1e12 / pk["bf16_tflops"],
+                "tensor_tflops": 4 * rows * H * I / (grouped_ms / 1e3) / 1e12,
+                "tensor_frac": 4 * rows * H * I / (grouped_ms / 1e3) / 1e12 / pk["bf16_tflops"],
             },
             "e2e": {"value": tokens_total / (total_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},

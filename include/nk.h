@@ -265,6 +265,51 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
                          void *out, int32_t out_dtype, int32_t *indices, float *weights,
                          void *workspace, size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------ MoE stages (expert parallelism)
+ * nk_moe_forward in three separable stages, so that the routed rows can be
+ * exchanged between ranks that own disjoint, contiguous ranges of experts
+ * (rank g owns experts [g*E/G, (g+1)*E/G)).  The reference has no
+ * distribution (one device, nemotron-kernels/src/device.rs:32-54); these
+ * split MoeLayer::forward_into (moe.rs:154-249) at its natural seams. */
+
+/* Stage 1 on the rank that owns the tokens: router GEMM, top-k routing
+ * (moe_routing.rs:168-216), expert plan and the gather of routed rows.
+ * indices/weights [tokens, top_k]; counts [E]; offsets [E+1] (exclusive
+ * prefix of counts); slot_pos [tokens*top_k]; routed_rows [tokens*top_k, H]
+ * bf16, ordered by expert, so the rows for each expert range are contiguous.
+ * workspace: nk_moe_dispatch_workspace_bytes. */
+nk_status nk_moe_dispatch_workspace_bytes(const nk_moe_layer *layer, int64_t tokens,
+                                          size_t *bytes);
+nk_status nk_moe_dispatch(const nk_moe_layer *layer, const uint16_t *x, int64_t tokens,
+                          int32_t *indices, float *weights, int32_t *counts, int32_t *offsets,
+                          int32_t *slot_pos, uint16_t *routed_rows, void *workspace,
+                          size_t workspace_bytes, void *stream);
+
+/* Stage 2 on the rank that owns the experts: the per-expert MLP
+ * relu2(row·upᵀ + b)·downᵀ + b (mlp.rs:157-211) over rows [n_rows, H] bf16
+ * laid out as n_segments back-to-back segments; segment s has seg_rows[s]
+ * rows for the layer's expert seg_expert[s] (device int32 arrays; seg_expert
+ * NULL = segment s is expert s).  `layer` describes the LOCAL experts only
+ * (experts = experts held here; router and shared expert unused).  out
+ * [n_rows, H] bf16 may alias rows.  n_segments <= 1024. */
+nk_status nk_moe_experts_workspace_bytes(const nk_moe_layer *layer, int64_t n_rows,
+                                         int32_t n_segments, size_t *bytes);
+nk_status nk_moe_experts(const nk_moe_layer *layer, const uint16_t *rows, int64_t n_rows,
+                         const int32_t *seg_expert, const int32_t *seg_rows, int32_t n_segments,
+                         uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The shared expert on the token rank: out [tokens, H] bf16 =
+ * relu2(x·shared_upᵀ + b)·shared_downᵀ + b; scratch [tokens, Is] bf16. */
+nk_status nk_moe_shared(const nk_moe_layer *layer, const uint16_t *x, int64_t tokens,
+                        uint16_t *scratch, uint16_t *out, void *stream);
+
+/* Stage 3 on the token rank: out[t] = shared[t] + Σ_r weights[t,r] ·
+ * expert_rows[slot_pos[t*top_k + r]], in rank order in f32 (moe.rs:195-246);
+ * shared may be NULL.  expert_rows are in the order routed_rows had. */
+nk_status nk_moe_combine(const uint16_t *expert_rows, const uint16_t *shared, const float *weights,
+                         const int32_t *slot_pos, int64_t tokens, int64_t hidden, int64_t top_k,
+                         void *out, int32_t out_dtype, void *stream);
+
 /* ---------------------------------------------------------------- tracing */
 
 /* Stage timing of nk_moe_forward (not in the reference, whose only timing is

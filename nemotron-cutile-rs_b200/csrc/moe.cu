@@ -12,29 +12,35 @@ namespace nk {
 constexpr int kMoeBN = 256;
 constexpr int kRouterMaxSplits = 16;
 
-// Grouped tile list: for each expert e with c_e routed rows, ceil(n_out/128)
-// feature tiles x ceil(c_e/BN) token tiles.  One block; E <= 1024.
-__global__ void build_tiles_kernel(const int32_t *__restrict__ counts,
-                                   const int32_t *__restrict__ offsets, int E, int n_out,
+// Grouped tile list over row segments: segment s holds seg_rows[s] contiguous
+// rows (segments back to back) for expert seg_expert[s] (identity when null).
+// Each segment gets ceil(n_out/128) feature tiles x ceil(rows/BN) token tiles.
+// One block of 1024 threads; n_seg <= 1024.
+__global__ void build_tiles_kernel(const int32_t *__restrict__ seg_rows,
+                                   const int32_t *__restrict__ seg_expert, int n_seg, int n_out,
                                    int bn, TcTile *__restrict__ tiles, int *__restrict__ count) {
-  __shared__ int sc[1024];
-  const int e = threadIdx.x;
+  __shared__ int tiles_sc[1024];
+  __shared__ int rows_sc[1024];
+  const int s = threadIdx.x;
   const int ft = (n_out + 127) / 128;
-  int c = e < E ? counts[e] : 0;
-  int tt = (c + bn - 1) / bn;
-  int mine = ft * tt;
-  sc[e] = mine;
+  const int c = s < n_seg ? seg_rows[s] : 0;
+  const int tt = (c + bn - 1) / bn;
+  const int mine = ft * tt;
+  tiles_sc[s] = mine;
+  rows_sc[s] = c;
   __syncthreads();
-  for (int o = 1; o < blockDim.x; o <<= 1) {
-    int v = e >= o ? sc[e - o] : 0;
+  for (int o = 1; o < blockDim.x; o <<= 1) {  // inclusive scans of tiles and rows
+    int v = s >= o ? tiles_sc[s - o] : 0;
+    int r = s >= o ? rows_sc[s - o] : 0;
     __syncthreads();
-    sc[e] += v;
+    tiles_sc[s] += v;
+    rows_sc[s] += r;
     __syncthreads();
   }
-  int base = sc[e] - mine;
-  if (e == blockDim.x - 1) *count = sc[e];
-  if (e >= E) return;
-  int off = offsets[e];
+  const int base = tiles_sc[s] - mine, off = rows_sc[s] - c;
+  if (s == blockDim.x - 1) *count = tiles_sc[s];
+  if (s >= n_seg) return;
+  const int e = seg_expert ? seg_expert[s] : s;
   for (int f = 0; f < ft; ++f)
     for (int t = 0; t < tt; ++t) {
       TcTile tile;
@@ -157,53 +163,80 @@ StageTimer &timer() {
   return t;
 }
 
-struct MoeWorkspace {
-  float *scores;
-  float *router_partial;  // [splits, T, E]
-  int32_t *idx;
-  float *w;
-  int32_t *counts, *offsets, *perm, *slot_pos, *plan_scratch;
-  TcTile *tiles_up, *tiles_down;
-  int *tile_counts;
-  uint16_t *xp;   // [slots, H]; reused for the routed expert outputs
-  uint16_t *hmid; // [slots, I]
-  uint16_t *s1;   // [T, Is]
-  uint16_t *sh;   // [T, H]
-  size_t bytes;
-};
-
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-MoeWorkspace carve(const nk_moe_layer &L, int64_t T, uint8_t *base) {
-  MoeWorkspace ws{};
+struct Carver {
+  uint8_t *base;
   size_t off = 0;
-  auto take = [&](size_t bytes) {
+  void *take(size_t bytes) {
     void *p = base ? base + off : nullptr;
     off += align256(bytes);
     return p;
-  };
-  const int64_t E = L.experts, K = L.top_k, H = L.hidden, I = L.inter, S = T * K;
-  ws.scores = (float *)take(sizeof(float) * T * E);
-  ws.router_partial = (float *)take(sizeof(float) * T * E * kRouterMaxSplits);
-  ws.idx = (int32_t *)take(sizeof(int32_t) * S);
-  ws.w = (float *)take(sizeof(float) * S);
-  ws.counts = (int32_t *)take(sizeof(int32_t) * E);
-  ws.offsets = (int32_t *)take(sizeof(int32_t) * (E + 1));
-  ws.perm = (int32_t *)take(sizeof(int32_t) * S);
-  ws.slot_pos = (int32_t *)take(sizeof(int32_t) * S);
-  ws.plan_scratch = (int32_t *)take(plan_scratch_bytes(S, E));
-  const int64_t max_tiles_up = ceil_div(I, 128) * (ceil_div(S, kMoeBN) + E);
-  const int64_t max_tiles_down = ceil_div(H, 128) * (ceil_div(S, kMoeBN) + E);
-  ws.tiles_up = (TcTile *)take(sizeof(TcTile) * max_tiles_up);
-  ws.tiles_down = (TcTile *)take(sizeof(TcTile) * max_tiles_down);
-  ws.tile_counts = (int *)take(sizeof(int) * 2);
-  ws.xp = (uint16_t *)take(2 * S * H);
-  ws.hmid = (uint16_t *)take(2 * S * I);
-  if (L.shared_inter > 0) {
-    ws.s1 = (uint16_t *)take(2 * T * L.shared_inter);
-    ws.sh = (uint16_t *)take(2 * T * H);
   }
-  ws.bytes = off;
+};
+
+// Scratch of the dispatch stage (router, routing, plan, gather).
+struct DispatchWs {
+  float *scores, *router_partial;
+  int32_t *perm, *plan_scratch;
+};
+DispatchWs carve_dispatch(const nk_moe_layer &L, int64_t T, Carver &c) {
+  const int64_t E = L.experts, S = T * L.top_k;
+  DispatchWs w;
+  w.scores = (float *)c.take(sizeof(float) * T * E);
+  w.router_partial = (float *)c.take(sizeof(float) * T * E * kRouterMaxSplits);
+  w.perm = (int32_t *)c.take(sizeof(int32_t) * S);
+  w.plan_scratch = (int32_t *)c.take(plan_scratch_bytes(S, E));
+  return w;
+}
+
+// Scratch of the grouped expert stage over R rows in n_seg segments.
+struct ExpertsWs {
+  TcTile *tiles_up, *tiles_down;
+  int *tile_counts;
+  uint16_t *hmid;  // [R, I]
+};
+ExpertsWs carve_experts(const nk_moe_layer &L, int64_t R, int64_t n_seg, Carver &c) {
+  ExpertsWs w;
+  const int64_t rows = R > 0 ? R : 1;
+  w.tiles_up = (TcTile *)c.take(sizeof(TcTile) * ceil_div(L.inter, 128) *
+                                (ceil_div(rows, kMoeBN) + n_seg));
+  w.tiles_down = (TcTile *)c.take(sizeof(TcTile) * ceil_div(L.hidden, 128) *
+                                  (ceil_div(rows, kMoeBN) + n_seg));
+  w.tile_counts = (int *)c.take(sizeof(int) * 2);
+  w.hmid = (uint16_t *)c.take(2 * rows * L.inter);
+  return w;
+}
+
+// Everything nk_moe_forward needs.
+struct MoeWorkspace {
+  DispatchWs d;
+  ExpertsWs x;
+  int32_t *idx, *counts, *offsets, *slot_pos;
+  float *w;
+  uint16_t *xp;  // [T*k, H] routed rows in expert order; reused for the expert outputs
+  uint16_t *s1;  // [T, Is]
+  uint16_t *sh;  // [T, H]
+  size_t bytes;
+};
+
+MoeWorkspace carve(const nk_moe_layer &L, int64_t T, uint8_t *base) {
+  MoeWorkspace ws{};
+  Carver c{base};
+  const int64_t E = L.experts, S = T * L.top_k, H = L.hidden;
+  ws.d = carve_dispatch(L, T, c);
+  ws.x = carve_experts(L, S, E, c);
+  ws.idx = (int32_t *)c.take(sizeof(int32_t) * S);
+  ws.w = (float *)c.take(sizeof(float) * S);
+  ws.counts = (int32_t *)c.take(sizeof(int32_t) * E);
+  ws.offsets = (int32_t *)c.take(sizeof(int32_t) * (E + 1));
+  ws.slot_pos = (int32_t *)c.take(sizeof(int32_t) * S);
+  ws.xp = (uint16_t *)c.take(2 * S * H);
+  if (L.shared_inter > 0) {
+    ws.s1 = (uint16_t *)c.take(2 * T * L.shared_inter);
+    ws.sh = (uint16_t *)c.take(2 * T * H);
+  }
+  ws.bytes = c.off;
   return ws;
 }
 
@@ -228,6 +261,21 @@ nk_status validate(const nk_moe_layer *L) {
   if (L->shared_inter > 0 && L->weight_kind == NK_W_INT8_ROW &&
       (!L->shared_up_scale || !L->shared_down_scale))
     return fail(NK_INVALID_PARAMS, "INT8_ROW shared expert needs scales");
+  return NK_OK;
+}
+
+// The grouped expert stage reads only the expert dimensions and weights.
+nk_status validate_experts(const nk_moe_layer *L) {
+  if (!L) return fail(NK_INVALID_SHAPE, "null layer");
+  if (L->hidden <= 0 || L->experts <= 0 || L->inter <= 0)
+    return fail(NK_INVALID_SHAPE, "hidden, experts and inter must be positive");
+  if (L->hidden % 8 || L->inter % 16)
+    return fail(NK_UNSUPPORTED, "hidden % 8 == 0 and inter % 16 == 0 required");
+  if (L->weight_kind != NK_W_BF16 && L->weight_kind != NK_W_INT8_ROW)
+    return fail(NK_UNSUPPORTED, "weight_kind");
+  if (!L->up_w || !L->down_w) return fail(NK_INVALID_PARAMS, "missing expert weights");
+  if (L->weight_kind == NK_W_INT8_ROW && (!L->up_scale || !L->down_scale))
+    return fail(NK_INVALID_PARAMS, "INT8_ROW weights need scales");
   return NK_OK;
 }
 
@@ -262,30 +310,18 @@ nk_status dense(int wk, const void *w, const float *row_scale, const float *bias
 
 }  // namespace
 
-nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void *out,
-                      int out_dtype, int32_t *indices, float *weights, void *workspace,
-                      size_t ws_bytes, cudaStream_t s) {
-  MoeWorkspace need = carve(L, T, nullptr);
-  if (!workspace || ws_bytes < need.bytes) {
-    nk_status st = fail(NK_WORKSPACE_TOO_SMALL, "workspace smaller than nk_moe_workspace_bytes");
-    tls_error().expected = need.bytes;
-    tls_error().actual = ws_bytes;
-    return st;
-  }
-  MoeWorkspace ws = carve(L, T, reinterpret_cast<uint8_t *>(workspace));
+// Router -> routing -> plan -> gather.  Outputs: indices/weights [T,k], counts [E],
+// offsets [E+1], slot_pos [T*k], xp [T*k, H] (routed rows in expert order).
+nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, int32_t *idx,
+                         float *rw, int32_t *counts, int32_t *offsets, int32_t *slot_pos,
+                         uint16_t *xp, const DispatchWs &ws, StageTimer &tm, cudaStream_t s) {
   int *err = device_error_ptr();
-  const int64_t E = L.experts, K = L.top_k, H = L.hidden, I = L.inter, S = T * K;
-  const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
-  int32_t *idx = indices ? indices : ws.idx;
-  float *rw = weights ? weights : ws.w;
+  const int64_t E = L.experts, K = L.top_k, H = L.hidden, S = T * K;
   nk_status st;
-
-  StageTimer &tm = timer();
-  tm.recorded = false;
   tm.mark(0, s);
-  // 1. router scores [T, E] f32: x · (hi + mid + lo)ᵀ.  K is split over CTAs into
-  //    f32 partial sums, reduced in split order; the bias is added after the
-  //    GEMM as linear.rs:333-339 does.
+  // router scores [T, E] f32: x · (hi + mid + lo)ᵀ.  K is split over CTAs into f32
+  // partial sums, reduced in split order; the bias is added after the GEMM as
+  // linear.rs:333-339 does.
   {
     const int64_t hp = ceil_div(H, 64) * 64;
     const int bn = T <= 64 ? 64 : 256;
@@ -320,30 +356,36 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
     if (st != NK_OK) return st;
   }
   tm.mark(1, s);
-  // 2. routing, 3. plan
   st = launch_route(ws.scores, T, (int)E, (int)K, L.route_mode, idx, rw, s);
   if (st != NK_OK) return st;
-  st = launch_plan(idx, S, (int)E, ws.counts, ws.offsets, ws.perm, ws.slot_pos, ws.plan_scratch, s);
-  if (st != NK_OK) return st;
-  build_tiles_kernel<<<1, 1024, 0, s>>>(ws.counts, ws.offsets, (int)E, (int)I, kMoeBN,
-                                        ws.tiles_up, ws.tile_counts);
-  build_tiles_kernel<<<1, 1024, 0, s>>>(ws.counts, ws.offsets, (int)E, (int)H, kMoeBN,
-                                        ws.tiles_down, ws.tile_counts + 1);
-  st = check_launch("build_tiles_kernel");
+  st = launch_plan(idx, S, (int)E, counts, offsets, ws.perm, slot_pos, ws.plan_scratch, s);
   if (st != NK_OK) return st;
   tm.mark(2, s);
-  // 4. gather routed token rows in expert order
-  {
-    const int warps = 8;
-    gather_rows_kernel<<<(unsigned)ceil_div(S, warps), warps * 32, 0, s>>>(
-        reinterpret_cast<const uint4 *>(x), ws.perm, S, (int)K, H / 8,
-        reinterpret_cast<uint4 *>(ws.xp));
-    st = check_launch("gather_rows_kernel");
-    if (st != NK_OK) return st;
-  }
+  const int warps = 8;
+  gather_rows_kernel<<<(unsigned)ceil_div(S, warps), warps * 32, 0, s>>>(
+      reinterpret_cast<const uint4 *>(x), ws.perm, S, (int)K, H / 8,
+      reinterpret_cast<uint4 *>(xp));
+  return check_launch("gather_rows_kernel");
+}
+
+// Grouped expert MLP over R rows laid out as n_seg back-to-back segments:
+// out[r] = relu2(rows[r] · up_eᵀ + b_up) · down_eᵀ + b_down for the segment's
+// expert e.  out may alias rows (rows are fully consumed before out is written).
+nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
+                        const int32_t *seg_expert, const int32_t *seg_rows, int n_seg,
+                        uint16_t *out, const ExpertsWs &ws, StageTimer &tm, cudaStream_t s) {
+  int *err = device_error_ptr();
+  const int64_t E = L.experts, H = L.hidden, I = L.inter;
+  const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
+  build_tiles_kernel<<<1, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, (int)I, kMoeBN,
+                                        ws.tiles_up, ws.tile_counts);
+  build_tiles_kernel<<<1, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, (int)H, kMoeBN,
+                                        ws.tiles_down, ws.tile_counts + 1);
+  nk_status st = check_launch("build_tiles_kernel");
+  if (st != NK_OK) return st;
+  if (R == 0) return NK_OK;
   tm.mark(3, s);
-  // 5. grouped up-projection + relu2: hmid[pos, :] = relu2(xp[pos] · up_eᵀ + b)
-  {
+  {  // grouped up-projection + relu2
     TcArgs a = base_args(err);
     a.tiles = ws.tiles_up;
     a.tile_count = ws.tile_counts;
@@ -353,48 +395,84 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
     a.row_scale = wk == WK_INT8 ? L.up_scale : nullptr;
     a.bias = L.up_b;
     a.relu2 = 1;
-    st = tc_gemm(wk, L.up_w, E * I, H, wk == WK_BF16 ? 2 * H : H, ws.xp, S, H, H, kMoeBN, a,
+    st = tc_gemm(wk, L.up_w, E * I, H, wk == WK_BF16 ? 2 * H : H, rows, R, H, H, kMoeBN, a,
                  num_sms(), s);
     if (st != NK_OK) return st;
   }
   tm.mark(4, s);
-  // 6. grouped down-projection: y[pos, :] = hmid[pos] · down_eᵀ + b  (into xp's storage)
-  uint16_t *yrouted = ws.xp;
-  {
+  {  // grouped down-projection
     TcArgs a = base_args(err);
     a.tiles = ws.tiles_down;
     a.tile_count = ws.tile_counts + 1;
     a.k_blocks = (int)ceil_div(I, 64);
-    a.y = yrouted;
+    a.y = out;
     a.ldy = H;
     a.row_scale = wk == WK_INT8 ? L.down_scale : nullptr;
     a.bias = L.down_b;
-    st = tc_gemm(wk, L.down_w, E * H, I, wk == WK_BF16 ? 2 * I : I, ws.hmid, S, I, I, kMoeBN, a,
+    st = tc_gemm(wk, L.down_w, E * H, I, wk == WK_BF16 ? 2 * I : I, ws.hmid, R, I, I, kMoeBN, a,
                  num_sms(), s);
-    if (st != NK_OK) return st;
   }
+  return st;
+}
+
+nk_status shared_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, uint16_t *s1,
+                       uint16_t *sh, cudaStream_t s) {
+  int *err = device_error_ptr();
+  const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
+  const int64_t Is = L.shared_inter, H = L.hidden;
+  nk_status st = dense(wk, L.shared_up_w, wk == WK_INT8 ? L.shared_up_scale : nullptr,
+                       L.shared_up_b, x, T, H, Is, s1, false, true, err, s);
+  if (st != NK_OK) return st;
+  return dense(wk, L.shared_down_w, wk == WK_INT8 ? L.shared_down_scale : nullptr,
+               L.shared_down_b, s1, T, Is, H, sh, false, false, err, s);
+}
+
+nk_status combine_stage(const uint16_t *y, const uint16_t *sh, const float *rw,
+                        const int32_t *slot_pos, int64_t T, int64_t H, int K, void *out,
+                        int out_dtype, cudaStream_t s) {
+  if (T == 0) return NK_OK;
+  if (out_dtype == NK_F32)
+    combine_kernel<true><<<(unsigned)T, 128, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(y), reinterpret_cast<const __nv_bfloat16 *>(sh),
+        rw, slot_pos, H, K, out);
+  else
+    combine_kernel<false><<<(unsigned)T, 128, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(y), reinterpret_cast<const __nv_bfloat16 *>(sh),
+        rw, slot_pos, H, K, out);
+  return check_launch("combine_kernel");
+}
+
+nk_status ws_too_small(size_t need, size_t have) {
+  nk_status st = fail(NK_WORKSPACE_TOO_SMALL, "workspace smaller than the *_workspace_bytes query");
+  tls_error().expected = need;
+  tls_error().actual = have;
+  return st;
+}
+
+nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void *out,
+                      int out_dtype, int32_t *indices, float *weights, void *workspace,
+                      size_t ws_bytes, cudaStream_t s) {
+  MoeWorkspace need = carve(L, T, nullptr);
+  if (!workspace || ws_bytes < need.bytes) return ws_too_small(need.bytes, ws_bytes);
+  MoeWorkspace ws = carve(L, T, reinterpret_cast<uint8_t *>(workspace));
+  const int64_t K = L.top_k, S = T * K;
+  int32_t *idx = indices ? indices : ws.idx;
+  float *rw = weights ? weights : ws.w;
+  StageTimer &tm = timer();
+  tm.recorded = false;
+  nk_status st = dispatch_stage(L, x, T, idx, rw, ws.counts, ws.offsets, ws.slot_pos, ws.xp,
+                                ws.d, tm, s);
+  if (st != NK_OK) return st;
+  // experts in expert order: one segment per expert, rows = counts[e]; outputs into xp
+  st = experts_stage(L, ws.xp, S, nullptr, ws.counts, (int)L.experts, ws.xp, ws.x, tm, s);
+  if (st != NK_OK) return st;
   tm.mark(5, s);
-  // 7. shared expert over all tokens
   if (L.shared_inter > 0) {
-    const int64_t Is = L.shared_inter;
-    st = dense(wk, L.shared_up_w, wk == WK_INT8 ? L.shared_up_scale : nullptr, L.shared_up_b, x,
-               T, H, Is, ws.s1, false, true, err, s);
-    if (st != NK_OK) return st;
-    st = dense(wk, L.shared_down_w, wk == WK_INT8 ? L.shared_down_scale : nullptr,
-               L.shared_down_b, ws.s1, T, Is, H, ws.sh, false, false, err, s);
+    st = shared_stage(L, x, T, ws.s1, ws.sh, s);
     if (st != NK_OK) return st;
   }
   tm.mark(6, s);
-  // 8. combine in rank order
-  if (out_dtype == NK_F32)
-    combine_kernel<true><<<(unsigned)T, 128, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16 *>(yrouted),
-        reinterpret_cast<const __nv_bfloat16 *>(ws.sh), rw, ws.slot_pos, H, (int)K, out);
-  else
-    combine_kernel<false><<<(unsigned)T, 128, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16 *>(yrouted),
-        reinterpret_cast<const __nv_bfloat16 *>(ws.sh), rw, ws.slot_pos, H, (int)K, out);
-  st = check_launch("combine_kernel");
+  st = combine_stage(ws.xp, ws.sh, rw, ws.slot_pos, T, L.hidden, (int)K, out, out_dtype, s);
   tm.mark(7, s);
   return st;
 }
@@ -423,6 +501,88 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
   if (out_dtype != NK_F32 && out_dtype != NK_BF16) return fail(NK_UNSUPPORTED, "out_dtype");
   st = moe_forward(*layer, x, tokens, out, out_dtype, indices, weights, workspace,
                    workspace_bytes, as_stream(stream));
+  return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_moe_dispatch_workspace_bytes(const nk_moe_layer *layer, int64_t tokens,
+                                          size_t *bytes) {
+  nk_status st = validate(layer);
+  if (st != NK_OK) return st;
+  if (tokens <= 0) return fail(NK_INVALID_ROW_COUNT, "row_count must be non-zero");
+  Carver c{nullptr};
+  carve_dispatch(*layer, tokens, c);
+  *bytes = c.off;
+  return ok();
+}
+
+nk_status nk_moe_dispatch(const nk_moe_layer *layer, const uint16_t *x, int64_t tokens,
+                          int32_t *indices, float *weights, int32_t *counts, int32_t *offsets,
+                          int32_t *slot_pos, uint16_t *routed_rows, void *workspace,
+                          size_t workspace_bytes, void *stream) {
+  nk_status st = validate(layer);
+  if (st != NK_OK) return st;
+  if (tokens <= 0) return fail(NK_INVALID_ROW_COUNT, "row_count must be non-zero");
+  if (tokens > (1 << 24)) return fail(NK_UNSUPPORTED, "too many tokens for one call");
+  Carver c{nullptr};
+  carve_dispatch(*layer, tokens, c);
+  if (!workspace || workspace_bytes < c.off) return ws_too_small(c.off, workspace_bytes);
+  Carver w{reinterpret_cast<uint8_t *>(workspace)};
+  DispatchWs ws = carve_dispatch(*layer, tokens, w);
+  StageTimer &tm = timer();
+  tm.recorded = false;
+  st = dispatch_stage(*layer, x, tokens, indices, weights, counts, offsets, slot_pos,
+                      routed_rows, ws, tm, as_stream(stream));
+  return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_moe_experts_workspace_bytes(const nk_moe_layer *layer, int64_t rows,
+                                         int32_t n_segments, size_t *bytes) {
+  nk_status st = validate_experts(layer);
+  if (st != NK_OK) return st;
+  if (rows < 0 || n_segments <= 0 || n_segments > 1024)
+    return fail(NK_INVALID_SHAPE, "rows >= 0 and 0 < n_segments <= 1024");
+  Carver c{nullptr};
+  carve_experts(*layer, rows, n_segments, c);
+  *bytes = c.off;
+  return ok();
+}
+
+nk_status nk_moe_experts(const nk_moe_layer *layer, const uint16_t *rows, int64_t n_rows,
+                         const int32_t *seg_expert, const int32_t *seg_rows, int32_t n_segments,
+                         uint16_t *out, void *workspace, size_t workspace_bytes, void *stream) {
+  nk_status st = validate_experts(layer);
+  if (st != NK_OK) return st;
+  if (n_rows < 0 || n_rows > (1 << 27) || n_segments <= 0 || n_segments > 1024)
+    return fail(NK_INVALID_SHAPE, "0 <= rows and 0 < n_segments <= 1024");
+  Carver c{nullptr};
+  carve_experts(*layer, n_rows, n_segments, c);
+  if (!workspace || workspace_bytes < c.off) return ws_too_small(c.off, workspace_bytes);
+  Carver w{reinterpret_cast<uint8_t *>(workspace)};
+  ExpertsWs ws = carve_experts(*layer, n_rows, n_segments, w);
+  StageTimer &tm = timer();
+  st = experts_stage(*layer, rows, n_rows, seg_expert, seg_rows, n_segments, out, ws, tm,
+                     as_stream(stream));
+  return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_moe_combine(const uint16_t *expert_rows, const uint16_t *shared, const float *weights,
+                         const int32_t *slot_pos, int64_t tokens, int64_t hidden, int64_t top_k,
+                         void *out, int32_t out_dtype, void *stream) {
+  if (tokens < 0 || hidden <= 0 || top_k <= 0 || top_k > 32 || hidden % 8)
+    return fail(NK_INVALID_SHAPE, "tokens >= 0, 0 < top_k <= 32, hidden % 8 == 0");
+  if (out_dtype != NK_F32 && out_dtype != NK_BF16) return fail(NK_UNSUPPORTED, "out_dtype");
+  nk_status st = combine_stage(expert_rows, shared, weights, slot_pos, tokens, hidden,
+                               (int)top_k, out, out_dtype, as_stream(stream));
+  return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_moe_shared(const nk_moe_layer *layer, const uint16_t *x, int64_t tokens,
+                        uint16_t *scratch, uint16_t *out, void *stream) {
+  nk_status st = validate(layer);
+  if (st != NK_OK) return st;
+  if (layer->shared_inter <= 0) return fail(NK_INVALID_PARAMS, "layer has no shared expert");
+  if (tokens <= 0) return fail(NK_INVALID_ROW_COUNT, "row_count must be non-zero");
+  st = shared_stage(*layer, x, tokens, scratch, out, as_stream(stream));
   return st == NK_OK ? ok() : st;
 }
 

@@ -103,6 +103,12 @@ _SIGS = {
     "nk_linear_pack_kn": (_i32, [_p, _i64, _i64, _p, _p]),
     "nk_moe_workspace_bytes": (_i32, [_p, _i64, _p]),
     "nk_moe_forward": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+    "nk_moe_dispatch_workspace_bytes": (_i32, [_p, _i64, _p]),
+    "nk_moe_dispatch": (_i32, [_p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "nk_moe_experts_workspace_bytes": (_i32, [_p, _i64, _i32, _p]),
+    "nk_moe_experts": (_i32, [_p, _p, _i64, _p, _p, _i32, _p, _p, _sz, _p]),
+    "nk_moe_shared": (_i32, [_p, _p, _i64, _p, _p, _p]),
+    "nk_moe_combine": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i32, _p]),
     "nk_set_stage_timing": (_i32, [_i32]),
     "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }
