@@ -186,6 +186,49 @@ def calibrate_tokens(fn, budget_s, max_tokens):
     return max(2, min(max_tokens, int(budget_s / per))), per
 
 
+def gemm_sweep(torch, nk, dev, reps=5):
+    """Y = X·Wᵀ, bf16 and int8-per-row weights, per shape the
+    mean of `reps` CUDA-event timings with an L2 flush before each; cuBLAS
+    (torch.matmul, bf16) timed the same way for context."""
+    pk = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    res = []
+
+    def timed(fn):
+        ts = []
+        for _ in range(reps + 1):
+            flush.zero_()
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b_.record()
+            b_.synchronize()
+            ts.append(a.elapsed_time(b_))
+        return sum(ts[1:]) / reps  # first call warms up
+
+    for (k, n) in [(4096, 4096), (4096, 21504), (21504, 4096)]:
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        q, s = nk.quantize_int8_row(w.float())
+        for m in (1, 16, 128, 2048, 8192):
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            row = {"m": m, "k": k, "n": n}
+            flops = 2 * m * n * k
+            for kind, wb, fn in (
+                    ("bf16", 2, lambda: nk.gemm(x, w, out_dtype=torch.bfloat16)),
+                    ("int8", 1, lambda: nk.gemm(x, q, kind="int8", scales=s,
+                                                out_dtype=torch.bfloat16)),
+                    ("cublas_bf16", 2, lambda: torch.matmul(x, w.t()))):
+                ms = timed(fn)
+                bytes_ = wb * n * k + 2 * m * k + 2 * m * n
+                row[kind] = {"us": round(ms * 1e3, 2), "tflops": round(flops / ms / 1e9, 1),
+                             "gbs": round(bytes_ / ms / 1e6, 1),
+                             "tensor_frac": round(flops / ms / 1e9 / pk["bf16_tflops"], 3),
+                             "hbm_frac": round(bytes_ / ms / 1e6 / pk["hbm_gbs"], 3)}
+            res.append(row)
+    return res
+
+
 class EpTimer:
     """Wraps nk_ep.NkBackend and times its stages with CUDA events on the
     current stream (dispatch, grouped experts, shared + combine); the rest of
@@ -446,6 +489,8 @@ def nk_arm(args):
             "clocks": clocks,
             "gpu_launches": 14 * args.steps * 2,
         }
+        if world == 1 and args.sweep:
+            line["gemm_sweep"] = gemm_sweep(torch, nk, dev)
         if world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
             sys.path.insert(0, os.path.join(ROOT, "oracle"))
             import oracle as orc
@@ -477,6 +522,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=T,
                     help="tokens per GPU (profiling captures use a smaller case)")
     ap.add_argument("--experts", type=int, default=E)
+    ap.add_argument("--sweep", action="store_true",
+                    help="also time the config-2 dense / int8 GEMM sweep (adds ~1 min)")
     ap.add_argument("--graph", action="store_true",
                     help="replay the forward as a captured CUDA graph (measured no faster "
                          "than eager launches: the step is device-bound)")

@@ -2,6 +2,9 @@
 // (f64 accumulation, SIMT) and the projection GEMMs, which dispatch to the
 // tcgen05 kernel (gemm_tc.cu) or, for shapes TMA cannot address (a row pitch
 // that is not a multiple of 16 bytes), to a plain CUDA kernel.
+#include <cmath>
+#include <cstdlib>
+
 #include "gemm_tc.h"
 
 namespace nk {
@@ -103,6 +106,49 @@ __global__ void proj_simt_kernel(const void *__restrict__ x, int x_f32,
     reinterpret_cast<__nv_bfloat16 *>(y)[idx] = __float2bfloat16_rn(o);
 }
 
+// y[m, n] = act(Σ_s partial[s][m, n] + bias[n]), partial sums added in split order.
+__global__ void splitk_reduce_kernel(const float *__restrict__ part, int splits, int64_t mn,
+                                     int64_t n, const float *__restrict__ bias, int relu2,
+                                     void *__restrict__ y, int y_f32) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= mn) return;
+  float acc = part[i];
+  for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[(int64_t)s * mn + i]);
+  if (bias) acc = __fadd_rn(acc, bias[i % n]);
+  if (relu2) acc = nk_relu2(acc);
+  if (y_f32)
+    reinterpret_cast<float *>(y)[i] = acc;
+  else
+    reinterpret_cast<__nv_bfloat16 *>(y)[i] = __float2bfloat16_rn(acc);
+}
+
+// K splits for a projection whose token dimension fits one tile (decode
+// shapes, HBM-bound).  Cost model in bytes moved: the weight stream stretched
+// by wave quantisation (units of work over whole waves of SMs), plus the f32
+// partial sums written and read back, plus a fixed cost for the extra reduce
+// launch.  Each split keeps >= 4 K blocks.
+static int choose_k_splits(int f_tiles, int t_tiles, int k_blocks, int sms, double w_bytes,
+                           int64_t m, int64_t n) {
+  if (t_tiles != 1) return 1;
+  auto cost = [&](int s) {
+    const double units = (double)f_tiles * s;
+    const double eff = units / (std::ceil(units / sms) * sms);
+    double c = w_bytes / eff;
+    if (s > 1) c += 8.0 * s * (double)m * (double)n + 20e6;
+    return c;
+  };
+  int best_s = 1;
+  double best = cost(1);
+  for (int s = 2; s <= 32 && k_blocks / s >= 4; ++s) {
+    const double c = cost(s);
+    if (c < best * 0.97) {
+      best = c;
+      best_s = s;
+    }
+  }
+  return best_s;
+}
+
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Shared driver for nk_gemm_bf16 / nk_gemm_w8row / nk_gemm_w4a.
@@ -146,45 +192,80 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
   int64_t x_k = k, ldx = k;
   int k_blocks = (int)ceil_div(k, 64);
   int w_period = 0;
+  const int64_t kp = ceil_div(k, 64) * 64;
   if (x_dtype == NK_F32) {
-    int64_t kp = ceil_div(k, 64) * 64;
-    void *buf = nullptr;
-    nk_status st = scratch((size_t)(m * 2 * kp * 2), &buf, stream);
+    w_period = (int)(kp / 64);
+    k_blocks = 2 * w_period;
+  }
+  const int bn = m <= 64 ? 64 : 256;
+  const int f_tiles = (int)ceil_div(n, 128), t_tiles = (int)ceil_div(m, bn);
+  const double w_bytes = (double)n * (double)k * (wk == WK_BF16 ? 2.0 : wk == WK_INT8 ? 1.0 : 0.5);
+  int splits = choose_k_splits(f_tiles, t_tiles, k_blocks, num_sms(), w_bytes, m, n);
+  if (const char *e = getenv("NK_SPLITK")) {  // tuning override: forced K split count
+    int v = atoi(e);
+    if (v >= 1 && v <= k_blocks) splits = v;
+  }
+  {  // every split gets at least one K block
+    const int per = (k_blocks + splits - 1) / splits;
+    splits = (k_blocks + per - 1) / per;
+  }
+
+  // scratch: [split activations (f32 x)] [split-K partial sums]
+  const size_t xsplit_bytes = x_dtype == NK_F32 ? (size_t)(m * 2 * kp * 2) : 0;
+  const size_t part_off = (xsplit_bytes + 255) & ~size_t(255);
+  const size_t part_bytes = splits > 1 ? (size_t)splits * m * n * 4 : 0;
+  uint8_t *buf = nullptr;
+  if (xsplit_bytes + part_bytes > 0) {
+    void *b = nullptr;
+    nk_status st = scratch(part_off + part_bytes, &b, stream);
     if (st != NK_OK) return st;
+    buf = reinterpret_cast<uint8_t *>(b);
+  }
+  if (x_dtype == NK_F32) {
     int64_t total = m * kp;
     split_f32_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, stream>>>(
         reinterpret_cast<const float *>(x), reinterpret_cast<__nv_bfloat16 *>(buf), m, k, kp);
-    st = check_launch("split_f32_kernel");
+    nk_status st = check_launch("split_f32_kernel");
     if (st != NK_OK) return st;
     xb = reinterpret_cast<const uint16_t *>(buf);
     x_k = 2 * kp;
     ldx = 2 * kp;
-    w_period = (int)(kp / 64);
-    k_blocks = 2 * w_period;
   }
 
-  const int bn = m <= 64 ? 64 : 256;
   TcArgs a{};
-  a.f_tiles = (int)ceil_div(n, 128);
-  a.t_tiles = (int)ceil_div(m, bn);
+  a.f_tiles = f_tiles;
+  a.t_tiles = t_tiles;
   a.n_features = (int)n;
   a.n_tokens = (int)m;
   a.k_blocks = k_blocks;
   a.w_k_period = w_period;
   a.x_k_period = 0;
-  a.y = y;
-  a.ldy = n;
-  a.y_f32 = y_dtype == NK_F32;
   a.w_scale = w_scale;
   a.row_scale = row_scale;
-  a.bias = bias;
-  a.relu2 = relu2;
   a.w_zero_point = zp;
   a.err = err;
-  int64_t tiles = (int64_t)a.f_tiles * a.t_tiles;
+  a.ldy = n;
+  if (splits > 1) {  // partial sums (row scale is linear, applied per split)
+    a.k_splits = splits;
+    a.split_stride = m * n;
+    a.y = buf + part_off;
+    a.y_f32 = 1;
+  } else {
+    a.y = y;
+    a.y_f32 = y_dtype == NK_F32;
+    a.bias = bias;
+    a.relu2 = relu2;
+  }
+  int64_t tiles = (int64_t)f_tiles * t_tiles * splits;
   int grid = (int)(tiles < num_sms() ? tiles : num_sms());
   int64_t ldw_bytes = wk == WK_BF16 ? k * 2 : (wk == WK_INT8 ? k : n / 2);
-  return tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream);
+  nk_status st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream);
+  if (st != NK_OK || splits == 1) return st;
+  const int64_t mn = m * n;
+  splitk_reduce_kernel<<<(unsigned)ceil_div(mn, 256), 256, 0, stream>>>(
+      reinterpret_cast<const float *>(buf + part_off), splits, mn, n, bias, relu2, y,
+      y_dtype == NK_F32);
+  return check_launch("splitk_reduce_kernel");
 }
 
 }  // namespace nk

@@ -275,31 +275,34 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
             row = idx >> 3;
             c = idx & 7;
             const uint2 src = *reinterpret_cast<const uint2 *>(raw + row * 64 + c * 8);
-            const uint32_t w[2] = {src.x, src.y};
+            // biased bytes u = v + 128 in [0, 255]; as_float(0x4B000000 | u) = 2^23 + u
+            const uint32_t w[2] = {src.x ^ 0x80808080u, src.y ^ 0x80808080u};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
               const uint32_t word = w[h >> 1];
-              const int sh = (h & 1) * 16;
-              float lo = (float)(int8_t)((word >> sh) & 0xFF);
-              float hi = (float)(int8_t)((word >> (sh + 8)) & 0xFF);
-              __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-              packed[h] = *reinterpret_cast<uint32_t *>(&p);
+              const int b0 = (h & 1) * 2;
+              const float lo = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 | b0)) -
+                               8388736.0f;  // 2^23 + 128
+              const float hi = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 | (b0 + 1))) -
+                               8388736.0f;
+              // exact small integers: the bf16 is the upper half of the f32
+              packed[h] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
             }
           } else {  // INT4 [K][128 features as 64 bytes]: element (k, n) -> byte k*64 + n/2
             row = idx & 127;  // feature
             c = idx >> 7;     // K chunk of 8
             const int sh = (row & 1) * 4;
+            const float bias = 8388608.0f + (float)args.w_zero_point;  // 2^23 + zp
             float vals[8];
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
-              const uint8_t b = raw[(c * 8 + kk) * 64 + (row >> 1)];
-              vals[kk] = (float)((int)((b >> sh) & 0xF) - args.w_zero_point);
+              const uint32_t b = raw[(c * 8 + kk) * 64 + (row >> 1)];
+              vals[kk] = __uint_as_float(0x4B000000u | ((b >> sh) & 0xFu)) - bias;
             }
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              __nv_bfloat162 p = __floats2bfloat162_rn(vals[2 * h], vals[2 * h + 1]);
-              packed[h] = *reinterpret_cast<uint32_t *>(&p);
-            }
+            for (int h = 0; h < 4; ++h)
+              packed[h] = __byte_perm(__float_as_uint(vals[2 * h]),
+                                      __float_as_uint(vals[2 * h + 1]), 0x7632);
           }
           *reinterpret_cast<uint4 *>(dst + row * 128 + ((c ^ (row & 7)) << 4)) =
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
