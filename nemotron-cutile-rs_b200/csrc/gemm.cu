@@ -232,8 +232,17 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
     ldx = 2 * kp;
   }
 
+  // Prefill shapes (more than one token tile) can run on CTA pairs: 256-feature
+  // tiles, each SM loading half of every token tile.  Measured no faster than
+  // single CTAs for bf16 weights and slower for int8 on B200, so opt-in
+  // (NK_PAIR=1).
+  static const bool pair_ok = [] {
+    const char *e = getenv("NK_PAIR");
+    return e && e[0] == '1';
+  }();
+  const int pair = (pair_ok && t_tiles >= 2 && bn == 256) ? 2 : 1;
   TcArgs a{};
-  a.f_tiles = f_tiles;
+  a.f_tiles = pair == 2 ? (int)ceil_div(n, 256) : f_tiles;
   a.t_tiles = t_tiles;
   a.n_features = (int)n;
   a.n_tokens = (int)m;
@@ -256,10 +265,11 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
     a.bias = bias;
     a.relu2 = relu2;
   }
-  int64_t tiles = (int64_t)f_tiles * t_tiles * splits;
-  int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  int64_t tiles = (int64_t)a.f_tiles * t_tiles * splits;
+  const int slots = num_sms() / pair;  // concurrent tiles
+  int grid = (int)(tiles < slots ? tiles : slots) * pair;
   int64_t ldw_bytes = wk == WK_BF16 ? k * 2 : (wk == WK_INT8 ? k : n / 2);
-  nk_status st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream);
+  nk_status st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream, pair);
   if (st != NK_OK || splits == 1) return st;
   const int64_t mn = m * n;
   splitk_reduce_kernel<<<(unsigned)ceil_div(mn, 256), 256, 0, stream>>>(

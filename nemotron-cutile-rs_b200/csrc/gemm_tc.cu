@@ -10,15 +10,16 @@ namespace nk {
 
 // Tile t of the launch.  With k_splits > 1 (dense grids only) consecutive tile
 // indices are the K splits of one output tile; every split covers >= 1 K block.
-template <int BN>
-__device__ __forceinline__ bool load_tile(const TcArgs &a, int t, TcTile &tile, int &k_begin,
+// FH = features per tile (128, or 256 for CTA pairs).
+template <int BN, int FH>
+__device__ __forceinline__ void load_tile(const TcArgs &a, int t, TcTile &tile, int &k_begin,
                                           int &k_count, int &split) {
   k_begin = 0;
   k_count = a.k_blocks;
   split = 0;
   if (a.tiles) {
     tile = a.tiles[t];
-    return true;
+    return;
   }
   if (a.k_splits > 1) {
     const int per = (a.k_blocks + a.k_splits - 1) / a.k_splits;
@@ -29,50 +30,63 @@ __device__ __forceinline__ bool load_tile(const TcArgs &a, int t, TcTile &tile, 
     k_count = left < per ? left : per;
   }
   int ft = t / a.t_tiles, tt = t - ft * a.t_tiles;
-  tile.w_row = ft * 128;
+  tile.w_row = ft * FH;
   tile.x_row = tt * BN;
-  tile.out_col0 = ft * 128;
-  int fv = a.n_features - ft * 128;
+  tile.out_col0 = ft * FH;
+  int fv = a.n_features - ft * FH;
   int tv = a.n_tokens - tt * BN;
-  tile.valid = ((fv > 128 ? 128 : fv) << 16) | (tv > BN ? BN : tv);
-  return true;
+  tile.valid = ((fv > FH ? FH : fv) << 16) | (tv > BN ? BN : tv);
 }
 
-template <int WK, int BN>
-__global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
+__device__ __forceinline__ uint32_t mma_n(int t_valid, int bn) {
+  uint32_t n = (uint32_t)((t_valid + 15) & ~15);
+  if (n < 16) n = 16;
+  if (n > (uint32_t)bn) n = bn;
+  return n;
+}
+
+template <int WK, int BN, int PAIR>
+__global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                    const __grid_constant__ CUtensorMap xmap, const TcArgs args) {
-  using Cfg = TcConfig<WK, BN>;
+  using Cfg = TcConfig<WK, BN, PAIR>;
   constexpr int S = Cfg::kStages;
+  constexpr int FH = Cfg::kFeatRows;
+  constexpr bool kQuant = WK != WK_BF16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *a_tiles = smem;                               // S x 16 KB (bf16, SW128)
-  uint8_t *b_tiles = a_tiles + S * Cfg::kABytes;         // S x BN*128
-  uint8_t *raw_tiles = b_tiles + S * Cfg::kBBytes;       // S x raw weight tile
+  uint8_t *a_tiles = smem;                          // S x 16 KB bf16 weight tiles (SW128)
+  uint8_t *b_tiles = a_tiles + S * Cfg::kABytes;    // S x kBRows*128 token tiles (SW128)
+  uint8_t *raw_tiles = b_tiles + S * Cfg::kBBytes;  // S x raw weight tiles (quantized)
   uint64_t *bars = reinterpret_cast<uint64_t *>(raw_tiles + S * Cfg::kRawBytes);
-  uint64_t *full = bars;            // TMA landed (weights raw/direct + activations)
-  uint64_t *empty = bars + S;       // MMA finished reading the stage
-  uint64_t *conv = bars + 2 * S;    // transform finished (quantized weights)
-  uint64_t *tfull = bars + 3 * S;   // accumulator ready (2)
-  uint64_t *tempty = bars + 3 * S + 2;  // accumulator drained (2)
-  uint64_t *drain = bars + 3 * S + 4;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
+  uint64_t *full = bars;            // leader: stage's TMA bytes landed (both CTAs)
+  uint64_t *empty = bars + S;       // MMAs finished reading the stage (every CTA)
+  uint64_t *conv = bars + 2 * S;    // leader: converted weight tiles ready (both CTAs)
+  uint64_t *rawfull = bars + 3 * S; // this CTA's raw weight tile landed (quantized)
+  uint64_t *tfull = bars + 4 * S;   // accumulator ready (2, every CTA)
+  uint64_t *tempty = tfull + 2;     // leader: accumulator drained (2)
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR == 2 ? cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x / PAIR, clusters = gridDim.x / PAIR;
   int *err = args.err;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 128);
+      mbar_init(&conv[s], 128 * PAIR);
+      mbar_init(&rawfull[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 128 * PAIR);
     }
     mbar_init(drain, 1);
     abort_flag = 0;
@@ -81,13 +95,22 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
     tma_prefetch_desc(&xmap);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    if (PAIR == 2) {
+      tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR == 2) cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
+  // shared::cluster addresses of the leader's barriers (PAIR == 2)
+  auto leader_bar = [&](uint64_t *b) -> uint32_t { return mapa_cta(smem_u32(b), 0); };
 
   const int num_tiles = args.tiles ? *args.tile_count
                                    : args.f_tiles * args.t_tiles *
@@ -101,30 +124,45 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = cluster_id; t < num_tiles && ok; t += clusters) {
         TcTile tile;
         int k_begin, k_count, split;
-        load_tile<BN>(args, t, tile, k_begin, k_count, split);
+        load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
+        const uint32_t n_mma = mma_n(tile.valid & 0xFFFF, BN);
+        const int a_row = tile.w_row + (int)rank * 128;
+        const int b_row = tile.x_row + (int)rank * (int)(n_mma / PAIR);
         for (int kk = 0; kk < k_count; ++kk) {
           if (*abort_v || !mbar_wait(&empty[stage], phase ^ 1, err)) {
             ok = false;
             break;
           }
           const int kb = k_begin + kk;
-          int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
-          int xkb = args.x_k_period > 0 ? kb % args.x_k_period : kb;
-          mbar_arrive_expect_tx(&full[stage], (WK == WK_BF16 ? Cfg::kABytes : Cfg::kRawBytes) +
-                                                  Cfg::kBBytes);
-          if (WK == WK_BF16)
-            tma_load_2d(a_tiles + stage * Cfg::kABytes, &wmap, &full[stage], wkb * 64,
-                        tile.w_row);
-          else if (WK == WK_INT8)
-            tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &full[stage], wkb * 64,
-                        tile.w_row);
-          else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
-            tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &full[stage],
-                        tile.w_row >> 1, wkb * 64);
-          tma_load_2d(b_tiles + stage * Cfg::kBBytes, &xmap, &full[stage], xkb * 64, tile.x_row);
+          const int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
+          const int xkb = args.x_k_period > 0 ? kb % args.x_k_period : kb;
+          // Token tile (and bf16 weight tile) complete on the leader's `full`;
+          // quantized raw weight tiles complete on this CTA's `rawfull`.
+          if (leader)
+            mbar_arrive_expect_tx(&full[stage],
+                                  PAIR * ((kQuant ? 0 : Cfg::kABytes) + Cfg::kBBytes));
+          if (kQuant) {
+            mbar_arrive_expect_tx(&rawfull[stage], Cfg::kRawBytes);
+            if (WK == WK_INT8)
+              tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &rawfull[stage], wkb * 64,
+                          a_row);
+            else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
+              tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &rawfull[stage],
+                          a_row >> 1, wkb * 64);
+          }
+          if (PAIR == 2) {
+            const uint32_t fb = leader_bar(&full[stage]);
+            if (!kQuant)
+              tma_load_2d_pair(a_tiles + stage * Cfg::kABytes, &wmap, fb, wkb * 64, a_row);
+            tma_load_2d_pair(b_tiles + stage * Cfg::kBBytes, &xmap, fb, xkb * 64, b_row);
+          } else {
+            if (!kQuant)
+              tma_load_2d(a_tiles + stage * Cfg::kABytes, &wmap, &full[stage], wkb * 64, a_row);
+            tma_load_2d(b_tiles + stage * Cfg::kBBytes, &xmap, &full[stage], xkb * 64, b_row);
+          }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) {
@@ -134,28 +172,28 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
         }
       }
       if (!ok) *abort_v = 1;
-      // Drain: every issued load must have landed before the CTA may exit.
+      // Drain: every issued load must have landed before the CTA may exit (the
+      // leader's `full` counts both CTAs' bytes; a peer's raw tiles its own rawfull).
       for (int s = 0; s < S; ++s)
-        if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1, err);
+        if (issued_mask & (1u << s)) {
+          if (leader) mbar_wait(&full[s], (issued_parity >> s) & 1, err);
+          if (kQuant) mbar_wait(&rawfull[s], (issued_parity >> s) & 1, err);
+        }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       const uint32_t a_base = smem_u32(a_tiles), b_base = smem_u32(b_tiles);
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = cluster_id; t < num_tiles && ok; t += clusters) {
         TcTile tile;
         int k_begin, k_count, split;
-        load_tile<BN>(args, t, tile, k_begin, k_count, split);
-        int t_valid = tile.valid & 0xFFFF;
-        uint32_t n_mma = (uint32_t)((t_valid + 15) & ~15);
-        if (n_mma < 16) n_mma = 16;
-        if (n_mma > BN) n_mma = BN;
-        const uint32_t idesc = idesc_bf16_f32(128, n_mma);
+        load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
+        const uint32_t idesc = idesc_bf16_f32(FH, mma_n(tile.valid & 0xFFFF, BN));
         if (*abort_v || !mbar_wait(&tempty[acc], acc_phase ^ 1, err)) {
           ok = false;
           break;
@@ -163,56 +201,79 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < k_count; ++kb) {
-          bool got = WK == WK_BF16 ? mbar_wait(&full[stage], phase, err)
-                                   : mbar_wait(&conv[stage], phase, err);
+          bool got = mbar_wait(&full[stage], phase, err);
+          if (kQuant && got) got = mbar_wait(&conv[stage], phase, err);
           if (*abort_v || !got) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint64_t ad = smem_desc_sw128(a_base + stage * Cfg::kABytes);
-          uint64_t bd = smem_desc_sw128(b_base + stage * Cfg::kBBytes);
+          const uint64_t ad = smem_desc_sw128(a_base + stage * Cfg::kABytes);
+          const uint64_t bd = smem_desc_sw128(b_base + stage * Cfg::kBBytes);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)  // 4 x K=16 steps, +32 bytes each (encoded >>4: +2)
-            tc_mma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
-          tc_commit(&empty[stage]);
+          for (int j = 0; j < 4; ++j) {  // 4 x K=16 steps, +32 bytes each (encoded >>4: +2)
+            if (PAIR == 2)
+              tc_mma_bf16_pair(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+            else
+              tc_mma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+          }
+          if (PAIR == 2) {
+            tc_commit_pair(mapa_cta(smem_u32(&empty[stage]), 0));
+            tc_commit_pair(mapa_cta(smem_u32(&empty[stage]), 1));
+          } else {
+            tc_commit(&empty[stage]);
+          }
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if (PAIR == 2) {
+          tc_commit_pair(mapa_cta(smem_u32(&tfull[acc]), 0));
+          tc_commit_pair(mapa_cta(smem_u32(&tfull[acc]), 1));
+        } else {
+          tc_commit(&tfull[acc]);
+        }
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
         }
       }
       if (!ok) *abort_v = 1;
-      // Drain: all issued MMAs complete before TMEM is released.
-      tc_commit(drain);
+      // Drain: all issued MMAs complete before TMEM is released (in both CTAs).
+      if (PAIR == 2) {
+        tc_commit_pair(mapa_cta(smem_u32(drain), 0));
+        tc_commit_pair(mapa_cta(smem_u32(drain), 1));
+      } else {
+        tc_commit(drain);
+      }
       mbar_wait(drain, 0, err);
+    } else if (lane == 0 && PAIR == 2) {
+      mbar_wait(drain, 0, err);  // peer: the leader's last MMAs wrote our TMEM too
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
-    const int i = quarter * 32 + lane;  // feature row within the tile
+    const int i = quarter * 32 + lane;  // feature row within this CTA's 128
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int t = cluster_id; t < num_tiles; t += clusters) {
       TcTile tile;
       int k_begin, k_count, split;
-      load_tile<BN>(args, t, tile, k_begin, k_count, split);
-      const int f_valid = tile.valid >> 16, t_valid = tile.valid & 0xFFFF;
+      load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
+      const int f_valid = (tile.valid >> 16) - (int)rank * 128, t_valid = tile.valid & 0xFFFF;
       // warp-uniform decision: tcgen05.ld below is .sync.aligned
-      const bool stop = __any_sync(0xffffffffu, *abort_v || !mbar_wait(&tfull[acc], acc_phase, err));
+      const bool stop =
+          __any_sync(0xffffffffu, *abort_v || !mbar_wait(&tfull[acc], acc_phase, err));
       if (stop) {
         *abort_v = 1;
         break;
       }
       tc_fence_after();
       const bool frow = i < f_valid;
-      const int f = tile.w_row + i;
+      const int fi = (int)rank * 128 + i;  // feature within the tile
+      const int f = tile.w_row + fi;
       float mul = args.w_scale, add = 0.0f;
       if (frow) {
         if (args.row_scale) mul *= args.row_scale[f];
@@ -231,9 +292,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
               float o = v[jj] * mul + add;
               if (args.relu2) o = nk_relu2(o);
               if (args.tok_scale) o *= args.tok_scale[tile.x_row + j];
-              const long long off =
-                  (long long)(tile.x_row + j) * args.ldy + tile.out_col0 + i +
-                  split * args.split_stride;
+              const long long off = (long long)(tile.x_row + j) * args.ldy + tile.out_col0 + fi +
+                                    split * args.split_stride;
               if (args.y_f32)
                 reinterpret_cast<float *>(args.y)[off] = o;
               else
@@ -243,24 +303,28 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if (PAIR == 2)
+        mbar_arrive_cluster(leader_bar(&tempty[acc]));
+      else
+        mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
-  } else if (WK != WK_BF16) {
+  } else if (kQuant) {
     // ------------------------------------------------------------ transform
     const int tid = threadIdx.x - 192;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      bool ok = true;
+    bool ok = true;
+    for (int t = cluster_id; t < num_tiles && ok; t += clusters) {
       TcTile tile;
       int k_begin, k_count, split;
-      load_tile<BN>(args, t, tile, k_begin, k_count, split);
+      load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
       for (int kb = 0; kb < k_count; ++kb) {
-        if (*abort_v || !mbar_wait(&full[stage], phase, err)) {
+        // the converted tile's slot is free once its stage's MMAs completed
+        if (*abort_v || !mbar_wait(&rawfull[stage], phase, err)) {
           ok = false;
           break;
         }
@@ -308,24 +372,35 @@ __global__ void __launch_bounds__(TcConfig<WK, BN>::kThreads, 1)
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&conv[stage]);
+        if (PAIR == 2)
+          mbar_arrive_cluster(leader_bar(&conv[stage]));
+        else
+          mbar_arrive(&conv[stage]);
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
         }
       }
-      if (!ok) {
-        *abort_v = 1;
-        break;
-      }
     }
+    if (!ok) *abort_v = 1;
   }
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR == 2) {
+    if (*abort_v) {  // let any copy still in flight from this CTA land (bounded)
+      const uint64_t t0 = nk_globaltimer();
+      while (nk_globaltimer() - t0 < 1000000ull) {
+      }
+    }
+    cluster_sync();  // no CTA exits while its peer may still arrive on its barriers
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if (PAIR == 2)
+      tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -375,20 +450,45 @@ nk_status make_map(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes, con
   return NK_OK;
 }
 
-template <int WK, int BN>
+template <int WK, int BN, int PAIR>
 nk_status launch_impl(const CUtensorMap &wm, const CUtensorMap &xm, const TcArgs &args, int grid,
                       cudaStream_t stream) {
-  using Cfg = TcConfig<WK, BN>;
+  using Cfg = TcConfig<WK, BN, PAIR>;
   static bool attr_done = false;  // benign race: setting the attribute twice is harmless
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WK, BN>,
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WK, BN, PAIR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmemBytes);
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(tc_gemm)");
     attr_done = true;
   }
-  tc_gemm_kernel<WK, BN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(wm, xm, args);
-  return check_launch("tc_gemm_kernel");
+  if (PAIR == 1) {
+    tc_gemm_kernel<WK, BN, 1><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(wm, xm, args);
+    return check_launch("tc_gemm_kernel");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WK, BN, PAIR>, wm, xm, args);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaLaunchKernelEx(tc_gemm pair)");
+  return check_launch("tc_gemm_kernel pair");
+}
+
+template <int WK>
+nk_status launch_kind(int bn, int pair, const CUtensorMap &wm, const CUtensorMap &xm,
+                      const TcArgs &args, int grid, cudaStream_t stream) {
+  if (pair == 2) return launch_impl<WK, 256, 2>(wm, xm, args, grid, stream);
+  return bn == 256 ? launch_impl<WK, 256, 1>(wm, xm, args, grid, stream)
+                   : launch_impl<WK, 64, 1>(wm, xm, args, grid, stream);
 }
 
 }  // namespace
@@ -396,7 +496,9 @@ nk_status launch_impl(const CUtensorMap &wm, const CUtensorMap &xm, const TcArgs
 // See gemm_tc.h.  w: bf16 [n_w_rows, ldw] / int8 [n_w_rows, ldw] / int4 bytes [K, N/2].
 nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ldw_bytes,
                   const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
-                  TcArgs args, int grid, cudaStream_t stream) {
+                  TcArgs args, int grid, cudaStream_t stream, int pair) {
+  if (pair == 2 && (bn != 256 || (grid & 1)))
+    return fail(NK_UNSUPPORTED, "CTA pairs need 256-token tiles and an even grid");
   CUtensorMap wm, xm;
   nk_status st;
   if (wk == WK_BF16)
@@ -410,17 +512,12 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
                   (uint64_t)w_k, (uint64_t)ldw_bytes, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != NK_OK) return st;
   st = make_map(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)x_k, (uint64_t)x_rows,
-                (uint64_t)ldx_elems * 2, 64, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
+                (uint64_t)ldx_elems * 2, 64, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NK_OK) return st;
   if (grid <= 0) return ok();
-  if (wk == WK_BF16)
-    return bn == 256 ? launch_impl<WK_BF16, 256>(wm, xm, args, grid, stream)
-                     : launch_impl<WK_BF16, 64>(wm, xm, args, grid, stream);
-  if (wk == WK_INT8)
-    return bn == 256 ? launch_impl<WK_INT8, 256>(wm, xm, args, grid, stream)
-                     : launch_impl<WK_INT8, 64>(wm, xm, args, grid, stream);
-  return bn == 256 ? launch_impl<WK_INT4KN, 256>(wm, xm, args, grid, stream)
-                   : launch_impl<WK_INT4KN, 64>(wm, xm, args, grid, stream);
+  if (wk == WK_BF16) return launch_kind<WK_BF16>(bn, pair, wm, xm, args, grid, stream);
+  if (wk == WK_INT8) return launch_kind<WK_INT8>(bn, pair, wm, xm, args, grid, stream);
+  return launch_kind<WK_INT4KN>(bn, pair, wm, xm, args, grid, stream);
 }
 
 }  // namespace nk

@@ -30,7 +30,7 @@ namespace nk {
 
 enum WeightKind { WK_BF16 = 0, WK_INT8 = 1, WK_INT4KN = 2 };
 
-struct TcTile {  // one output tile: 128 features x up to BN tokens
+struct TcTile {  // one output tile: 128 (256 for CTA pairs) features x up to BN tokens
   int w_row;     // first weight row (feature) in the weight tensor map
   int x_row;     // first activation row in the activation tensor map
   int valid;     // (f_valid << 16) | t_valid
@@ -66,10 +66,14 @@ struct WeightTile {
   static constexpr int kRawBytes = WK == WK_BF16 ? 0 : (WK == WK_INT8 ? 128 * 64 : 64 * 64);
 };
 
-template <int WK, int BN>
+// PAIR = 1: one CTA computes 128 features x BN tokens.
+// PAIR = 2: a cluster of two CTAs computes 256 features x BN tokens with
+// tcgen05.mma.cta_group::2; each CTA holds 128 weight rows and BN/2 token rows.
+template <int WK, int BN, int PAIR = 1>
 struct TcConfig {
-  static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
-  static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
+  static constexpr int kABytes = 128 * 128;         // 128 weight rows x 64 bf16
+  static constexpr int kBRows = BN / PAIR;          // token rows loaded per CTA
+  static constexpr int kBBytes = kBRows * 128;      // kBRows x 64 bf16
   static constexpr int kRawBytes = WeightTile<WK>::kRawBytes;
   static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
   static constexpr int kStages0 = (224 * 1024) / kStageBytes;
@@ -77,6 +81,7 @@ struct TcConfig {
   static constexpr int kThreads = WK == WK_BF16 ? 192 : 320;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
+  static constexpr int kFeatRows = 128 * PAIR;      // features per output tile
 };
 
 }  // namespace nk

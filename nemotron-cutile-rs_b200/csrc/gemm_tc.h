@@ -9,8 +9,11 @@ namespace nk {
 // the reference [K,N] nibble layout (w_rows = N features, w_k = K rows,
 // ldw_bytes = N/2).  Activations (B): bf16 [x_rows, x_k], pitch ldx_elems.
 // bn: 256 or 64 token rows per tile.  grid: CTAs (persistent over tiles).
+// pair = 2: clusters of two CTAs share 256-feature tiles (tcgen05 cta_group::2);
+// needs bn = 256, an even grid, and tiles of 256 features (f_tiles / tile lists
+// built with 256-row feature tiles).
 nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ldw_bytes,
                   const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
-                  TcArgs args, int grid, cudaStream_t stream);
+                  TcArgs args, int grid, cudaStream_t stream, int pair = 1);
 
 }  // namespace nk

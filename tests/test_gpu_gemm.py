@@ -149,3 +149,30 @@ def test_gemm_large_against_torch_fp32(cuda):
         err = ((y - ref).abs().max() / ref.abs().max()).item()
         assert err <= FP32_TOL, (m, k, n, err)
     nk.device_status()
+
+
+def test_gemm_cta_pair_path_matches_single_cta(cuda):
+    """The tcgen05 cta_group::2 path (opt-in, NK_PAIR=1) in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path.insert(0, 'nemotron-cutile-rs_b200');"
+        "import torch, nk;"
+        "g = torch.Generator(device='cuda').manual_seed(0);"
+        "x = torch.randn(700, 512, device='cuda', generator=g).bfloat16();"
+        "w = (torch.randn(520, 512, device='cuda', generator=g) * 0.02).bfloat16();"
+        "q, s = nk.quantize_int8_row(w.float());"
+        "ref = x.float() @ w.float().t();"
+        "y = nk.gemm(x, w);"
+        "e1 = ((y - ref).abs().max() / ref.abs().max()).item();"
+        "ref8 = x.float() @ (q.float() * s[:, None]).t();"
+        "y8 = nk.gemm(x, q, kind='int8', scales=s);"
+        "e2 = ((y8 - ref8).abs().max() / ref8.abs().max()).item();"
+        "nk.device_status(); print(e1, e2)")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True,
+                       env=dict(os.environ, NK_PAIR="1"), timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    e1, e2 = map(float, r.stdout.split())
+    assert e1 <= FP32_TOL and e2 <= FP32_TOL
