@@ -243,10 +243,10 @@ class EpTimer:
         e.record()
         self.ev.append((name, e))
 
-    def dispatch(self, x):
+    def dispatch(self, x, gather=True):
         self.ev = []
         self._mark("start")
-        r = self.be.dispatch(x)
+        r = self.be.dispatch(x, gather=gather)
         self._mark("dispatch")
         return r
 
@@ -256,13 +256,19 @@ class EpTimer:
         self._mark("experts")
         return r
 
+    def experts_into(self, rows, seg_expert, seg_rows, out):
+        self._mark("exchange_in")
+        r = self.be.experts_into(rows, seg_expert, seg_rows, out)
+        self._mark("experts")
+        return r
+
     def shared(self, x):
-        self._mark("exchange_out")
-        return self.be.shared(x)
+        return self.be.shared(x)  # may run on a side stream: not timed separately
 
     def combine(self, *a):
+        self._mark("exchange_out")
         r = self.be.combine(*a)
-        self._mark("shared_combine")
+        self._mark("combine")
         return r
 
     def step_times(self):
@@ -305,7 +311,7 @@ def reference_arm(args):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print_json(line)
     return 0
 
 
@@ -314,8 +320,10 @@ def config_dict(args, impl):
             "hidden": H, "experts": E, "top_k": K, "expert_inter": I, "shared_inter": IS,
             "routing": "sigmoid top-6 renormalised", "weights": args.weights,
             "parallelism": (f"expert-parallel x{args.gpus}: {E // max(args.gpus, 1)} experts per "
-                            "rank, NCCL all-to-all-v of routed rows" if args.gpus > 1
-                            else "single GPU, all experts"),
+                            "rank, routed rows exchanged by "
+                            + ("NVLink peer stores (libnk kernels)" if args.exchange == "peer"
+                               else "NCCL all-to-all-v")
+                            if args.gpus > 1 else "single GPU, all experts"),
             "l2": "256 MiB buffer written between timed steps",
             "launch": "CUDA graph of the nk_moe_forward call" if args.graph
                       else "eager launches",
@@ -355,7 +363,8 @@ def nk_arm(args):
         fwd = lambda: layer.forward(x, out=out, indices=idx)  # noqa: E731
         fwd_e2e = lambda: layer.forward(xin, out=out, indices=idx)  # noqa: E731
     else:
-        from nk_ep import ExpertParallelMoe, NkBackend, local_expert_slice
+        from nk_ep import (ExpertParallelMoe, NkBackend, PeerExpertParallelMoe,
+                           local_expert_slice)
 
         el = E // world
         lw = nk.MoeWeights(hidden=H, experts=el, top_k=1, inter=I, shared_inter=0,
@@ -368,7 +377,10 @@ def nk_arm(args):
                            down_scale=None if w.down_scale is None else
                            w.down_scale.reshape(E, H)[rank * el:(rank + 1) * el].reshape(-1))
         ep_timer = EpTimer(NkBackend(w, lw), torch)
-        ep = ExpertParallelMoe(ep_timer, E, H, K)
+        if args.exchange == "nccl":
+            ep = ExpertParallelMoe(ep_timer, E, H, K)
+        else:
+            ep = PeerExpertParallelMoe(ep_timer, E, H, K, max_tokens=T)
 
         def fwd():
             out.copy_(ep.forward(x)[0])
@@ -451,7 +463,8 @@ def nk_arm(args):
             rows = T * K
         else:  # this rank's experts and the rows it received in the last step
             active = E // world
-            rows = int(sum(ep.last_exchange["received_rows"]))
+            rows = (int(sum(ep.last_exchange["received_rows"])) if args.exchange == "nccl"
+                    else int(ep.total.item()))
         expert_w_bytes = active * 2 * I * H * wbytes_per
         act_bytes = rows * H * 2 + 2 * rows * I * 2 + rows * H * 2
         grouped_bytes = expert_w_bytes + act_bytes
@@ -505,13 +518,24 @@ def nk_arm(args):
                           "MoeLayer::forward_into (f64-accumulate GEMM loops) on the GPU arm's "
                           "weights, single thread, gathered rows (the reference itself runs "
                           "every selected expert over all rows)"}
-        print(json.dumps(line), flush=True)
+        print_json(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
 
 
 def main():
+    # Libraries (NCCL) may print to stdout; the contract is one JSON line there.
+    # Keep the real stdout for that line and send everything else to stderr.
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+    global print_json
+    json_out = os.fdopen(json_fd, "w")
+
+    def print_json(obj):
+        json_out.write(json.dumps(obj) + "\n")
+        json_out.flush()
+
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -522,6 +546,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=T,
                     help="tokens per GPU (profiling captures use a smaller case)")
     ap.add_argument("--experts", type=int, default=E)
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="expert-parallel row exchange: NVLink peer stores (libnk kernels) "
+                         "or NCCL all-to-all-v")
     ap.add_argument("--sweep", action="store_true",
                     help="also time the config-2 dense / int8 GEMM sweep (adds ~1 min)")
     ap.add_argument("--graph", action="store_true",

