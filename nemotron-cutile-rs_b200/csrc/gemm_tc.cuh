@@ -77,7 +77,10 @@ struct TcConfig {
   static constexpr int kRawBytes = WeightTile<WK>::kRawBytes;
   static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
   static constexpr int kStages0 = (224 * 1024) / kStageBytes;
-  static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+#ifndef NK_STAGES_MAX
+#define NK_STAGES_MAX 8
+#endif
+  static constexpr int kStages = kStages0 > NK_STAGES_MAX ? NK_STAGES_MAX : kStages0;
   static constexpr int kThreads = WK == WK_BF16 ? 192 : 320;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
