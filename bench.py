@@ -445,8 +445,9 @@ def nk_arm(args):
 
     total_ms = sum(step_ms)
     total_e2e = sum(e2e_ms)
-    if world == 1:
-        grouped_ms = (stage_sum.get("up_proj", 0.0) + stage_sum.get("down_proj", 0.0)) / args.steps
+    if world == 1:  # up/down stages; the shared expert runs beside them when overlapped
+        grouped_ms = (stage_sum.get("up_proj", 0.0) + stage_sum.get("down_proj", 0.0) +
+                      stage_sum.get("shared_expert", 0.0)) / args.steps
     else:
         grouped_ms = stage_sum.get("experts", 0.0) / args.steps
     if world > 1:
@@ -468,6 +469,10 @@ def nk_arm(args):
         expert_w_bytes = active * 2 * I * H * wbytes_per
         act_bytes = rows * H * 2 + 2 * rows * I * 2 + rows * H * 2
         grouped_bytes = expert_w_bytes + act_bytes
+        grouped_flops = 4 * rows * H * I
+        if world == 1:  # the shared expert shares the window: its weights and activations
+            grouped_bytes += 2 * IS * H * wbytes_per + T * H * 2 + 2 * T * IS * 2 + T * H * 2
+            grouped_flops += 4 * T * H * IS
         routed, shared, router = layer_flops(T)
         tokens_total = T * world * args.steps
         value = tokens_total / (total_ms / 1e3)
@@ -476,7 +481,7 @@ def nk_arm(args):
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
             with open(tp) as f:
-                traffic = json.load(f).get(f"moe_grouped_{args.weights}")
+                traffic = json.load(f).get(f"moe_grouped_{args.weights}") if world == 1 else None
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -489,13 +494,16 @@ def nk_arm(args):
                                         / 1e12) / pk["bf16_tflops"],
             "stages_ms": {k2: v / args.steps for k2, v in stage_sum.items()},
             "roofline": {
-                "kernel": "tc_gemm_kernel grouped up + down projections (2 launches per step)",
+                "kernel": ("tc_gemm_kernel: grouped expert up/down projections with the shared "
+                           "expert's two GEMMs running beside them (4 launches per step)"
+                           if world == 1 else
+                           "tc_gemm_kernel: grouped up/down projections of this rank's experts"),
                 "bound": "hbm", "achieved": ach_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": ach_gbs / pk["hbm_gbs"], "traffic": traffic,
                 "peak_source": pk["source"],
                 "algorithmic_bytes_per_step": grouped_bytes,
-                "tensor_tflops": 4 * rows * H * I / (grouped_ms / 1e3) / 1e12,
-                "tensor_frac": 4 * rows * H * I / (grouped_ms / 1e3) / 1e12 / pk["bf16_tflops"],
+                "tensor_tflops": grouped_flops / (grouped_ms / 1e3) / 1e12,
+                "tensor_frac": grouped_flops / (grouped_ms / 1e3) / 1e12 / pk["bf16_tflops"],
             },
             "e2e": {"value": tokens_total / (total_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
