@@ -229,6 +229,52 @@ def gemm_sweep(torch, nk, dev, reps=5):
     return res
 
 
+def tp_projections(torch, dev, world, reps=10):
+    """BASELINE config 4's GEMMs at T=8192: Mamba2 in_proj [4096 -> 18560]
+    column-parallel and out_proj [8192 -> 4096] row-parallel with one NCCL
+    all-reduce of f32 partials, over the `world` ranks (strong scaling)."""
+    import torch.distributed as dist
+
+    import nk
+    import nk_tp
+
+    T_, HM, NIN, KOUT = 8192, 4096, 18560, 8192
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(T_, HM, device=dev, generator=g).to(torch.bfloat16)
+    w_in = (torch.randn(NIN, HM, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w_out = (torch.randn(HM, KOUT, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    z = torch.randn(T_, KOUT, device=dev, generator=g).to(torch.bfloat16)
+    if world > 1:
+        col, row = nk_tp.ColumnParallelLinear(w_in), nk_tp.RowParallelLinear(w_out)
+        a, b_ = row.k_range
+        zs = z[:, a:b_].contiguous()
+        step = lambda: (col.forward(x), row.forward(zs))  # noqa: E731
+    else:
+        step = lambda: (nk.gemm(x, w_in, out_dtype=torch.bfloat16),  # noqa: E731
+                        nk.gemm(z, w_out, out_dtype=torch.bfloat16))
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for _ in range(reps):
+        step()
+    e_.record()
+    e_.synchronize()
+    ms = s_.elapsed_time(e_) / reps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    flops = 2 * T_ * HM * NIN + 2 * T_ * KOUT * HM
+    return {"config": "Mamba2 in_proj 4096->18560 (column-parallel) + out_proj 8192->4096 "
+                      "(row-parallel, NCCL all-reduce), T=8192 bf16",
+            "ms": round(ms, 4), "tflops_total": round(flops / ms / 1e9, 1),
+            "tflops_per_gpu": round(flops / ms / 1e9 / world, 1), "n_gpus": world}
+
+
 class EpTimer:
     """Wraps nk_ep.NkBackend and times its stages with CUDA events on the
     current stream (dispatch, grouped experts, shared + combine); the rest of
@@ -455,6 +501,7 @@ def nk_arm(args):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms, total_e2e, _ = t.tolist()
 
+    tp_result = tp_projections(torch, dev, world) if args.tp else None
     if rank == 0:
         pk = peaks()
         wbytes_per = 1 if args.weights == "int8" else 2
@@ -510,6 +557,8 @@ def nk_arm(args):
             "clocks": clocks,
             "gpu_launches": 14 * args.steps * 2,
         }
+        if args.tp:
+            line["tp_projections"] = tp_result
         if world == 1 and args.sweep:
             line["gemm_sweep"] = gemm_sweep(torch, nk, dev)
         if world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
@@ -557,6 +606,8 @@ def main():
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel row exchange: NVLink peer stores (libnk kernels) "
                          "or NCCL all-to-all-v")
+    ap.add_argument("--tp", action="store_true",
+                    help="also time config 4's tensor-parallel projections")
     ap.add_argument("--sweep", action="store_true",
                     help="also time the config-2 dense / int8 GEMM sweep (adds ~1 min)")
     ap.add_argument("--graph", action="store_true",
