@@ -207,7 +207,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
             ok = false;
             break;
           }
-          tc_fence_after();
+          // (the mbarrier wait orders the TMA-written operands for the MMA; no
+          // tcgen05 fence is needed per stage)
           const uint64_t ad = smem_desc_sw128(a_base + stage * Cfg::kABytes);
           const uint64_t bd = smem_desc_sw128(b_base + stage * Cfg::kBBytes);
 #pragma unroll
