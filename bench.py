@@ -188,24 +188,33 @@ def calibrate_tokens(fn, budget_s, max_tokens):
 
 def gemm_sweep(torch, nk, dev, reps=5):
     """Y = X·Wᵀ, bf16 and int8-per-row weights, per shape the
-    mean of `reps` CUDA-event timings with an L2 flush before each; cuBLAS
-    (torch.matmul, bf16) timed the same way for context."""
+    mean of `reps` CUDA-event timings of a graph replay with an L2 flush before
+    each; cuBLAS (torch.matmul, bf16) timed the same way for context."""
     pk = peaks()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     g = torch.Generator(device=dev).manual_seed(5)
     res = []
 
     def timed(fn):
+        """Device time of one call: the call is captured once into a CUDA graph
+        (after a warm-up call that sizes libnk's scratch) and the graph is
+        replayed, so host-side launch overhead is excluded for both libnk and
+        cuBLAS."""
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
         ts = []
         for _ in range(reps + 1):
             flush.zero_()
             a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            fn()
+            graph.replay()
             b_.record()
             b_.synchronize()
             ts.append(a.elapsed_time(b_))
-        return sum(ts[1:]) / reps  # first call warms up
+        return sum(ts[1:]) / reps
 
     for (k, n) in [(4096, 4096), (4096, 21504), (21504, 4096)]:
         w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
