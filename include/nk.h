@@ -49,7 +49,10 @@ enum {
   NK_UNSUPPORTED = 7,        /* a layout/dtype combination libnk does not implement */
   NK_DEVICE_ERROR = 8,       /* *::DeviceError(String) */
   NK_TIMEOUT = 9,            /* a bounded device-side wait gave up */
-  NK_WORKSPACE_TOO_SMALL = 10
+  NK_WORKSPACE_TOO_SMALL = 10,
+  NK_INVALID_DELTA_T = 11,   /* SsmError::InvalidDeltaT (index = (b*seq + t)*C + ch, value = dt) */
+  NK_EMPTY_INPUT = 12,       /* RmsNormError::EmptyInput */
+  NK_NEGATIVE_EPSILON = 13   /* RmsNormError::NegativeEpsilon (value = epsilon) */
 };
 
 typedef struct nk_error_info {
@@ -369,6 +372,93 @@ nk_status nk_set_stage_timing(int32_t enable);
 nk_status nk_moe_stage_times(float *ms, int32_t capacity, int32_t *count);
 
 #if defined(__GNUC__)
+/* ===================================================== Mamba2 glue ====
+ * The stages of Mamba2Mixer::forward (nemotron-nn/src/mamba2.rs:264-375)
+ * between the input projections and out_proj: causal depthwise conv (with
+ * the conv cache as history), SiLU, selective scan, gated RMSNorm.  All f32,
+ * as in the reference.  Pointers are device pointers. */
+
+/* Replaces depthwise_causal_conv1d_into_host / depthwise_causal_conv1d
+ * (nemotron-kernels/src/conv1d.rs:78-124, 325-345).  input [seq, channels],
+ * weights [channels, kernel_size] (tap j reads step t-j with weight
+ * kernel_size-1-j), f64 accumulation.  Errors: InvalidShape (channels or
+ * kernel_size 0), LengthMismatch input / weights / output; seq 0 is valid. */
+nk_status nk_conv1d(const float *input, size_t input_len, const float *weights,
+                    size_t weights_len, int64_t seq, int64_t channels, int64_t kernel_size,
+                    float *out, size_t out_len, void *stream);
+
+/* Batched conv as Mamba2Mixer::forward runs it (mamba2.rs:276-312): per batch,
+ * history = the K-1 cached steps (prefix, [batch, K-1, channels]) or zeros;
+ * y = conv(history ++ x) without the history rows, optionally SiLU'd
+ * (activations.rs:95-97); state_out (NULL or [batch, K-1, channels], may be
+ * the prefix itself) receives the last K-1 steps of history ++ x. */
+typedef struct nk_conv_args {
+  int64_t batch, seq, channels, kernel_size;
+  const float *x; int64_t ld_x;   /* x[(b*seq + t)*ld_x + ch] */
+  const float *weights;           /* [channels, kernel_size] */
+  const float *prefix;            /* NULL: zero history */
+  int32_t silu;
+  float *y; int64_t ld_y;         /* y[(b*seq + t)*ld_y + ch] */
+  float *state_out;               /* NULL: not written */
+  int32_t f32_accumulate;         /* 0: f64 as the reference (bit-exact); 1: f32 FMA chain */
+} nk_conv_args;
+nk_status nk_conv1d_ex(const nk_conv_args *args, void *stream);
+
+/* Replaces selective_scan_into_host / selective_scan (nemotron-kernels/src/
+ * ssm.rs:123-175, 614-624): reference layouts input/delta_t [seq, C],
+ * a [C, S], b/c [seq, C, S], d [C] or NULL, initial_state [C, S] or NULL;
+ * writes out [seq, C] and final_state [C, S].  Validation order and errors
+ * as ssm.rs:177-288 (InvalidShape, LengthMismatch, InvalidDeltaT for the
+ * first (t, ch) in t-major order whose dt is non-finite or negative).  The
+ * dt check reads back one word, so this call synchronises `stream`. */
+nk_status nk_selective_scan(const float *input, size_t input_len, const float *delta_t,
+                            size_t delta_t_len, const float *a, size_t a_len, const float *b,
+                            size_t b_len, const float *c, size_t c_len, const float *d,
+                            size_t d_len, const float *initial_state, size_t initial_state_len,
+                            float delta_bias, int32_t apply_softplus, int64_t seq,
+                            int64_t channels, int64_t states, float *out, size_t out_len,
+                            float *final_state, size_t final_state_len, void *stream);
+
+/* Strided / shared-parameter form of the same recurrence.  Channel ch of a
+ * group shares a parameter row: with every *_group = 1, a_per_state = 1 and
+ * ld_bc = C*S this is exactly the reference layout; the Mamba2 layout (one
+ * dt, A and D per head, B/C per group, all read in place from the fused
+ * in_proj output) sets dt_group = a_group = d_group = head_dim,
+ * a_per_state = 0, bc_group = C / ngroups. */
+typedef struct nk_scan_args {
+  int64_t batch, seq, channels, states;
+  const float *x; int64_t ld_x;                       /* x[(b*seq + t)*ld_x + ch] */
+  const float *dt; int64_t ld_dt; int32_t dt_group;   /* dt[(b*seq + t)*ld_dt + ch/dt_group] */
+  const float *a; int32_t a_group; int32_t a_per_state;
+      /* a[(ch/a_group)*states + s] if a_per_state, else a[ch/a_group] */
+  const float *b; const float *c; int64_t ld_bc; int32_t bc_group;
+      /* b[(b*seq + t)*ld_bc + (ch/bc_group)*states + s] */
+  const float *d; int32_t d_group;                    /* NULL or d[ch/d_group] */
+  const float *initial_state;                         /* NULL or [batch, C, S] */
+  float delta_bias; int32_t softplus;
+  float *y; int64_t ld_y;                             /* y[(b*seq + t)*ld_y + ch] */
+  float *final_state;                                 /* NULL or [batch, C, S]; may alias initial_state */
+  int32_t check_delta_t;  /* 1: synchronise and report InvalidDeltaT; 0: no readback (graph capture) */
+} nk_scan_args;
+nk_status nk_selective_scan_ex(const nk_scan_args *args, void *stream);
+
+/* Replaces rms_norm_into_host (gate NULL) / gated_rms_norm_into_host
+ * (nemotron-kernels/src/rms_norm.rs:64-106): one vector of `len`.
+ * Errors: EmptyInput, LengthMismatch weight / gate / output, NegativeEpsilon. */
+nk_status nk_rms_norm(const float *input, size_t len, const float *weight, size_t weight_len,
+                      const float *gate, size_t gate_len, float epsilon, float *out,
+                      size_t out_len, void *stream);
+
+/* Row-wise contract of rms_norm / gated_rms_norm (rms_norm.rs:291-360) and
+ * gated_rms_norm_rows (mamba2.rs:567-586): each of `rows` rows of `width`
+ * normalised alone.  out_dtype NK_DTYPE_F32 or NK_DTYPE_BF16 (round to
+ * nearest even, to feed out_proj directly).  gate may be NULL. */
+enum { NK_DTYPE_F32 = 0, NK_DTYPE_BF16 = 1 };
+nk_status nk_rms_norm_rows(const float *x, int64_t rows, int64_t width, int64_t ld_x,
+                           const float *weight, size_t weight_len, const float *gate,
+                           int64_t ld_gate, float epsilon, void *out, int64_t ld_out,
+                           int32_t out_dtype, void *stream);
+
 #pragma GCC visibility pop
 #endif
 

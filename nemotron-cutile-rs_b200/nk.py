@@ -20,11 +20,12 @@ LIB_PATH = os.path.join(_HERE, "libnk.so")
 # status codes (nk.h)
 OK, INVALID_SHAPE, LENGTH_MISMATCH, INVALID_PARAMS, INT4_OUT_OF_RANGE = 0, 1, 2, 3, 4
 NON_FINITE_INPUT, INVALID_ROW_COUNT, UNSUPPORTED, DEVICE_ERROR, TIMEOUT = 5, 6, 7, 8, 9
-WORKSPACE_TOO_SMALL = 10
+WORKSPACE_TOO_SMALL, INVALID_DELTA_T, EMPTY_INPUT, NEGATIVE_EPSILON = 10, 11, 12, 13
 STATUS_NAMES = {
     0: "Ok", 1: "InvalidShape", 2: "LengthMismatch", 3: "InvalidParams",
     4: "Int4OutOfRange", 5: "NonFiniteInput", 6: "InvalidRowCount", 7: "Unsupported",
-    8: "DeviceError", 9: "Timeout", 10: "WorkspaceTooSmall",
+    8: "DeviceError", 9: "Timeout", 10: "WorkspaceTooSmall", 11: "InvalidDeltaT",
+    12: "EmptyInput", 13: "NegativeEpsilon",
 }
 F32, BF16 = 0, 1
 EPI_RELU2 = 1
@@ -62,6 +63,30 @@ class NkMoeLayer(_c.Structure):
         ("down_w", _p), ("down_scale", _p), ("down_b", _p),
         ("shared_up_w", _p), ("shared_up_scale", _p), ("shared_up_b", _p),
         ("shared_down_w", _p), ("shared_down_scale", _p), ("shared_down_b", _p),
+    ]
+
+
+class NkConvArgs(_c.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seq", _i64), ("channels", _i64), ("kernel_size", _i64),
+        ("x", _p), ("ld_x", _i64), ("weights", _p), ("prefix", _p), ("silu", _i32),
+        ("y", _p), ("ld_y", _i64), ("state_out", _p), ("f32_accumulate", _i32),
+    ]
+
+
+class NkScanArgs(_c.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seq", _i64), ("channels", _i64), ("states", _i64),
+        ("x", _p), ("ld_x", _i64),
+        ("dt", _p), ("ld_dt", _i64), ("dt_group", _i32),
+        ("a", _p), ("a_group", _i32), ("a_per_state", _i32),
+        ("b", _p), ("c", _p), ("ld_bc", _i64), ("bc_group", _i32),
+        ("d", _p), ("d_group", _i32),
+        ("initial_state", _p),
+        ("delta_bias", _f), ("softplus", _i32),
+        ("y", _p), ("ld_y", _i64),
+        ("final_state", _p),
+        ("check_delta_t", _i32),
     ]
 
 
@@ -116,6 +141,14 @@ _SIGS = {
     "nk_ep_plan": (_i32, [_p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p]),
     "nk_ep_dispatch": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p, _p, _i32, _p, _p]),
     "nk_ep_return": (_i32, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p]),
+    "nk_conv1d": (_i32, [_p, _sz, _p, _sz, _i64, _i64, _i64, _p, _sz, _p]),
+    "nk_conv1d_ex": (_i32, [_p, _p]),
+    "nk_selective_scan": (_i32, [_p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz,
+                                 _f, _i32, _i64, _i64, _i64, _p, _sz, _p, _sz, _p]),
+    "nk_selective_scan_ex": (_i32, [_p, _p]),
+    "nk_rms_norm": (_i32, [_p, _sz, _p, _sz, _p, _sz, _f, _p, _sz, _p]),
+    "nk_rms_norm_rows": (_i32, [_p, _i64, _i64, _i64, _p, _sz, _p, _i64, _f, _p, _i64, _i32,
+                                _p]),
     "nk_set_stage_timing": (_i32, [_i32]),
     "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }
@@ -355,3 +388,97 @@ class MoeLayer:
 
 def device_status(stream=None) -> None:
     call("nk_device_status", stream_ptr(stream))
+
+
+# ------------------------------------------------------------- Mamba2 glue
+def _numel(t) -> int:
+    return 0 if t is None else t.numel()
+
+
+def conv1d(inp, weights, seq: int, channels: int, kernel_size: int, out=None, stream=None):
+    """depthwise_causal_conv1d (conv1d.rs:78-124, 325-345) on device f32 tensors."""
+    import torch
+
+    _require_cuda(inp, weights, out)
+    if out is None:
+        out = torch.empty(max(seq * channels, 1), dtype=torch.float32, device=inp.device)
+        out_len = seq * channels
+    else:
+        out_len = out.numel()
+    call("nk_conv1d", ptr(inp), inp.numel(), ptr(weights), weights.numel(), seq, channels,
+         kernel_size, ptr(out), out_len, stream_ptr(stream))
+    return out[:out_len]
+
+
+def conv1d_ex(x, weights, batch: int, seq: int, channels: int, kernel_size: int, *,
+              ld_x=None, prefix=None, silu=False, y=None, ld_y=None, state_out=None,
+              f32_accumulate=False, stream=None):
+    """Batched causal conv with conv-cache history and fused SiLU (mamba2.rs:276-312)."""
+    import torch
+
+    _require_cuda(x, weights, prefix, y, state_out)
+    if y is None:
+        y = torch.empty(batch * seq, channels, dtype=torch.float32, device=x.device)
+        ld_y = channels
+    a = NkConvArgs(batch, seq, channels, kernel_size, ptr(x), ld_x or channels, ptr(weights),
+                   ptr(prefix), 1 if silu else 0, ptr(y), ld_y or channels, ptr(state_out),
+                   1 if f32_accumulate else 0)
+    call("nk_conv1d_ex", ctypes.byref(a), stream_ptr(stream))
+    return y
+
+
+def selective_scan(inp, delta_t, a, b, c, seq: int, channels: int, states: int, *, d=None,
+                   initial_state=None, delta_bias: float = 0.0, softplus: bool = False,
+                   out=None, final_state=None, stream=None):
+    """selective_scan (ssm.rs:123-175, 614-624).  Returns (values, final_state)."""
+    import torch
+
+    _require_cuda(inp, delta_t, a, b, c, d, initial_state, out, final_state)
+    dev = inp.device
+    ol = seq * channels if out is None else out.numel()
+    fl = channels * states if final_state is None else final_state.numel()
+    if out is None:
+        out = torch.empty(max(ol, 1), dtype=torch.float32, device=dev)
+    if final_state is None:
+        final_state = torch.empty(max(fl, 1), dtype=torch.float32, device=dev)
+    call("nk_selective_scan", ptr(inp), inp.numel(), ptr(delta_t), delta_t.numel(), ptr(a),
+         a.numel(), ptr(b), b.numel(), ptr(c), c.numel(), ptr(d), _numel(d),
+         ptr(initial_state), _numel(initial_state), delta_bias, 1 if softplus else 0, seq,
+         channels, states, ptr(out), ol, ptr(final_state), fl, stream_ptr(stream))
+    return out[:ol], final_state[:fl]
+
+
+def selective_scan_ex(args: NkScanArgs, stream=None) -> None:
+    """Strided / shared-parameter scan (nk_selective_scan_ex); args hold device pointers."""
+    call("nk_selective_scan_ex", ctypes.byref(args), stream_ptr(stream))
+
+
+def rms_norm(inp, weight, epsilon: float, gate=None, out=None, stream=None):
+    """rms_norm_into_host / gated_rms_norm_into_host (rms_norm.rs:64-106) on device."""
+    import torch
+
+    _require_cuda(inp, weight, gate, out)
+    n = inp.numel()
+    ol = n if out is None else out.numel()
+    if out is None:
+        out = torch.empty(max(n, 1), dtype=torch.float32, device=inp.device)
+    call("nk_rms_norm", ptr(inp), n, ptr(weight), weight.numel(), ptr(gate), _numel(gate),
+         epsilon, ptr(out), ol, stream_ptr(stream))
+    return out[:ol]
+
+
+def rms_norm_rows(x, weight, epsilon: float, gate=None, out_dtype: int = F32, out=None,
+                  stream=None):
+    """Row-wise (gated) RMSNorm (rms_norm.rs:291-360, mamba2.rs:567-586); x is [rows, width]
+    (row stride taken from the tensor), gate likewise or None."""
+    import torch
+
+    _require_cuda(x, weight, gate, out)
+    rows, width = x.shape
+    if out is None:
+        out = torch.empty(rows, width, device=x.device,
+                          dtype=torch.bfloat16 if out_dtype == BF16 else torch.float32)
+    call("nk_rms_norm_rows", ptr(x), rows, width, x.stride(0), ptr(weight), weight.numel(),
+         ptr(gate), gate.stride(0) if gate is not None else 0, epsilon, ptr(out),
+         out.stride(0), out_dtype, stream_ptr(stream))
+    return out

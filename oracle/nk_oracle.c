@@ -465,3 +465,120 @@ float orc_bf16_to_f32(uint16_t b) {
   memcpy(&f, &u, 4);
   return f;
 }
+
+/* ------------------------------------------------------------ Mamba2 glue */
+
+/* activations.rs:64-66 */
+float orc_silu(float x) { return x * orc_sigmoid(x); }
+
+/* conv1d.rs:78-124, validation order conv1d.rs:126-158. */
+int orc_conv1d(const float *input, size_t input_len, const float *weights, size_t weights_len,
+               size_t seq, size_t channels, size_t kernel_size, float *out, size_t out_len,
+               orc_error *err) {
+  if (channels == 0 || kernel_size == 0) return set_err(err, ORC_INVALID_SHAPE);
+  if (input_len != seq * channels) return len_err(err, "input", seq * channels, input_len);
+  if (weights_len != channels * kernel_size)
+    return len_err(err, "weights", channels * kernel_size, weights_len);
+  if (out_len != seq * channels) return len_err(err, "output", seq * channels, out_len);
+  for (size_t t = 0; t < seq; ++t)
+    for (size_t ch = 0; ch < channels; ++ch) {
+      double acc = 0.0;
+      for (size_t tap = 0; tap < kernel_size && tap <= t; ++tap)
+        acc += (double)input[(t - tap) * channels + ch] *
+               (double)weights[ch * kernel_size + (kernel_size - 1 - tap)];
+      out[t * channels + ch] = (float)acc;
+    }
+  return set_err(err, ORC_OK);
+}
+
+/* ssm.rs:257-263: threshold 20, otherwise ln(1 + e^v) in f32. */
+static float orc_softplus(float v) { return v > 20.0f ? v : logf(1.0f + expf(v)); }
+
+/* ssm.rs:123-175 */
+int orc_selective_scan(const float *input, size_t input_len, const float *delta_t,
+                       size_t delta_t_len, const float *a, size_t a_len, const float *b,
+                       size_t b_len, const float *c, size_t c_len, const float *d, size_t d_len,
+                       const float *initial_state, size_t initial_state_len, float delta_bias,
+                       int apply_softplus, size_t seq, size_t channels, size_t states,
+                       float *out, size_t out_len, float *final_state, size_t final_state_len,
+                       orc_error *err) {
+  if (seq == 0 || channels == 0 || states == 0) return set_err(err, ORC_INVALID_SHAPE);
+  const size_t n = seq * channels, sm = channels * states, bl = seq * channels * states;
+  if (input_len != n) return len_err(err, "input", n, input_len);
+  if (delta_t_len != n) return len_err(err, "delta_t", n, delta_t_len);
+  if (a_len != sm) return len_err(err, "a", sm, a_len);
+  if (b_len != bl) return len_err(err, "b", bl, b_len);
+  if (c_len != bl) return len_err(err, "c", bl, c_len);
+  if (d && d_len != channels) return len_err(err, "d", channels, d_len);
+  if (initial_state && initial_state_len != sm)
+    return len_err(err, "initial_state", sm, initial_state_len);
+  if (out_len != n) return len_err(err, "output", n, out_len);
+  if (final_state_len != sm) return len_err(err, "final_state", sm, final_state_len);
+
+  if (initial_state)
+    memcpy(final_state, initial_state, sizeof(float) * sm);
+  else
+    memset(final_state, 0, sizeof(float) * sm);
+
+  for (size_t t = 0; t < seq; ++t)
+    for (size_t ch = 0; ch < channels; ++ch) {
+      const size_t i = t * channels + ch;
+      const float x = input[i];
+      const float raw = delta_t[i] + delta_bias;
+      const float dt = apply_softplus ? orc_softplus(raw) : raw;
+      if (!isfinite(dt) || dt < 0.0f) {
+        if (err) {
+          err->code = ORC_INVALID_DELTA_T;
+          err->index = i;
+          err->value = dt;
+        }
+        return ORC_INVALID_DELTA_T;
+      }
+      double acc = 0.0;
+      for (size_t s = 0; s < states; ++s) {
+        const size_t m = ch * states + s, o = i * states + s;
+        const float transition = expf(dt * a[m]);
+        const float mix = dt * b[o] * x;
+        const float next = transition * final_state[m] + mix;
+        final_state[m] = next;
+        acc += (double)(c[o] * next);
+      }
+      if (d) acc += (double)(d[ch] * x);
+      out[i] = (float)acc;
+    }
+  return set_err(err, ORC_OK);
+}
+
+/* rms_norm.rs:64-144: lengths (validate_lengths :146-183), then rms_host
+ * :108-124 (empty, negative epsilon, f64 mean square cast to f32, + eps,
+ * sqrt), reciprocal, x * scale * weight (* gate). */
+int orc_rms_norm(const float *input, size_t len, const float *weight, size_t weight_len,
+                 const float *gate, size_t gate_len, float epsilon, float *out, size_t out_len,
+                 orc_error *err) {
+  if (len == 0) return set_err(err, ORC_EMPTY_INPUT);
+  if (weight_len != len) return len_err(err, "weight", len, weight_len);
+  if (gate && gate_len != len) return len_err(err, "gate", len, gate_len);
+  if (out_len != len) return len_err(err, "output", len, out_len);
+  if (epsilon < 0.0f) {
+    if (err) {
+      err->code = ORC_NEGATIVE_EPSILON;
+      err->value = epsilon;
+    }
+    return ORC_NEGATIVE_EPSILON;
+  }
+  double sum = 0.0;
+  for (size_t i = 0; i < len; ++i) sum += (double)input[i] * (double)input[i];
+  const float denom = sqrtf((float)(sum / (double)len) + epsilon);
+  const float scale = 1.0f / denom;
+  for (size_t i = 0; i < len; ++i) {
+    float v = input[i] * scale * weight[i];
+    if (gate) v *= gate[i];
+    out[i] = v;
+  }
+  return set_err(err, ORC_OK);
+}
+
+/* activations.rs:95-97 (silu_in_place_host). */
+void orc_silu_in_place(float *values, size_t n) {
+  for (size_t i = 0; i < n; ++i) values[i] = orc_silu(values[i]);
+}

@@ -37,6 +37,9 @@ enum {
   ORC_INT4_OUT_OF_RANGE = 4,
   ORC_NON_FINITE_INPUT = 5,
   ORC_INVALID_ROW_COUNT = 6,
+  ORC_INVALID_DELTA_T = 11,  /* ssm.rs SsmError::InvalidDeltaT; index = t*C + ch */
+  ORC_EMPTY_INPUT = 12,      /* rms_norm.rs RmsNormError::EmptyInput */
+  ORC_NEGATIVE_EPSILON = 13, /* rms_norm.rs RmsNormError::NegativeEpsilon; value = eps */
 };
 
 typedef struct orc_error {
@@ -123,6 +126,37 @@ int orc_moe(size_t hidden, size_t experts, size_t top_k, size_t inter, size_t sh
  * restatement, not the reference). */
 void orc_gemm_rows(const float *lhs, const float *rhs, size_t m, size_t k, size_t n,
                    size_t row_limit, float *out, int threads);
+
+/* ---- Mamba2 glue (the stages between in_proj and out_proj) ---- */
+
+/* activations.rs:64-66: x * sigmoid(x). */
+float orc_silu(float x);
+/* activations.rs:95-97 */
+void orc_silu_in_place(float *values, size_t n);
+
+/* conv1d.rs:78-124 (+ validate_shape :126-158): depthwise causal conv,
+ * input [seq, C], weights [C, K] applied reversed (tap j reads t-j with
+ * weights[ch*K + K-1-j]), f64 accumulation, zero history before t = 0. */
+int orc_conv1d(const float *input, size_t input_len, const float *weights, size_t weights_len,
+               size_t seq, size_t channels, size_t kernel_size, float *out, size_t out_len,
+               orc_error *err);
+
+/* ssm.rs:123-175 (+ validate_params :177-211, validate_shape :239-245,
+ * softplus :257-263, validated_delta_t :265-288).  d and initial_state may be
+ * NULL.  On InvalidDeltaT, err->index = t*C + ch and err->value = dt. */
+int orc_selective_scan(const float *input, size_t input_len, const float *delta_t,
+                       size_t delta_t_len, const float *a, size_t a_len, const float *b,
+                       size_t b_len, const float *c, size_t c_len, const float *d, size_t d_len,
+                       const float *initial_state, size_t initial_state_len, float delta_bias,
+                       int apply_softplus, size_t seq, size_t channels, size_t states,
+                       float *out, size_t out_len, float *final_state, size_t final_state_len,
+                       orc_error *err);
+
+/* rms_norm.rs:64-144: rms_norm_into_host (gate NULL) / gated_rms_norm_into_host.
+ * One vector; the row-wise contract applies this per row. */
+int orc_rms_norm(const float *input, size_t len, const float *weight, size_t weight_len,
+                 const float *gate, size_t gate_len, float epsilon, float *out, size_t out_len,
+                 orc_error *err);
 
 /* bf16 helpers shared by the tests: round-to-nearest-even f32 -> bf16. */
 uint16_t orc_f32_to_bf16(float x);

@@ -235,3 +235,124 @@ def sigmoid(x: float) -> float:
 
 def relu2(x: float) -> float:
     return lib().orc_relu2(x)
+
+
+# ------------------------------------------------------------ Mamba2 glue
+
+ERR_NAMES.update({11: "InvalidDeltaT", 12: "EmptyInput", 13: "NegativeEpsilon"})
+
+
+def silu(x: float) -> float:
+    f = lib().orc_silu
+    f.restype, f.argtypes = ctypes.c_float, [ctypes.c_float]
+    return f(x)
+
+
+def silu_array(values):
+    """silu_in_place_host (activations.rs:95-97) through the C restatement (libm expf)."""
+    v = np.array(np.asarray(values, dtype=np.float32).reshape(-1), dtype=np.float32, copy=True)
+    if v.size:
+        lib().orc_silu_in_place(_p(v), ctypes.c_size_t(v.size))
+    return v
+
+
+def conv1d(inp, weights, seq, channels, kernel_size, input_len=None, weights_len=None,
+           out_len=None):
+    """depthwise_causal_conv1d_into_host (conv1d.rs:78-124)."""
+    x = _f32(np.asarray(inp).reshape(-1)) if np.asarray(inp).size else np.zeros(1, np.float32)
+    w = _f32(np.asarray(weights).reshape(-1)) if np.asarray(weights).size else np.zeros(1, np.float32)
+    il = np.asarray(inp).size if input_len is None else input_len
+    wl = np.asarray(weights).size if weights_len is None else weights_len
+    ol = seq * channels if out_len is None else out_len
+    out = np.zeros(max(ol, 1), np.float32)
+    err = OrcError()
+    rc = lib().orc_conv1d(_p(x), ctypes.c_size_t(il), _p(w), ctypes.c_size_t(wl),
+                          ctypes.c_size_t(seq), ctypes.c_size_t(channels),
+                          ctypes.c_size_t(kernel_size), _p(out), ctypes.c_size_t(ol),
+                          ctypes.byref(err))
+    _check(rc, err)
+    return out[:ol]
+
+
+def _arr(a):
+    if a is None:
+        return None, 0
+    a = np.asarray(a, dtype=np.float32).reshape(-1)
+    return (np.ascontiguousarray(a) if a.size else np.zeros(1, np.float32)), a.size
+
+
+def selective_scan(inp, delta_t, a, b, c, seq, channels, states, d=None, initial_state=None,
+                   delta_bias=0.0, softplus=False, out_len=None, final_state_len=None):
+    """selective_scan_into_host (ssm.rs:123-175).  Returns (values, final_state)."""
+    args = [_arr(v) for v in (inp, delta_t, a, b, c, d, initial_state)]
+    ol = seq * channels if out_len is None else out_len
+    fl = channels * states if final_state_len is None else final_state_len
+    out = np.zeros(max(ol, 1), np.float32)
+    fin = np.zeros(max(fl, 1), np.float32)
+    err = OrcError()
+    flat = []
+    for arr, n in args:
+        flat += [_p(arr), ctypes.c_size_t(n)]
+    rc = lib().orc_selective_scan(*flat, ctypes.c_float(delta_bias), ctypes.c_int(int(softplus)),
+                                  ctypes.c_size_t(seq), ctypes.c_size_t(channels),
+                                  ctypes.c_size_t(states), _p(out), ctypes.c_size_t(ol),
+                                  _p(fin), ctypes.c_size_t(fl), ctypes.byref(err))
+    _check(rc, err)
+    return out[:ol], fin[:fl]
+
+
+def rms_norm(inp, weight, epsilon, gate=None, out_len=None):
+    """rms_norm_into_host / gated_rms_norm_into_host (rms_norm.rs:64-144)."""
+    (x, n), (w, wn), (g, gn) = _arr(inp), _arr(weight), _arr(gate)
+    ol = n if out_len is None else out_len
+    out = np.zeros(max(ol, 1), np.float32)
+    err = OrcError()
+    rc = lib().orc_rms_norm(_p(x), ctypes.c_size_t(n), _p(w), ctypes.c_size_t(wn), _p(g),
+                            ctypes.c_size_t(gn), ctypes.c_float(epsilon), _p(out),
+                            ctypes.c_size_t(ol), ctypes.byref(err))
+    _check(rc, err)
+    return out[:ol]
+
+
+def rms_norm_rows(inp, weight, epsilon, row_width, gate=None):
+    """Row-wise contract (rms_norm.rs:224-252): each row of `row_width` normalised alone."""
+    x = np.asarray(inp, np.float32).reshape(-1, row_width)
+    g = None if gate is None else np.asarray(gate, np.float32).reshape(-1, row_width)
+    return np.concatenate([rms_norm(x[r], weight, epsilon, None if g is None else g[r])
+                           for r in range(x.shape[0])])
+
+
+def mamba2_glue(x_proj, delta_t, b, c, gate, conv_weights, ssm_a, norm_weight, epsilon,
+                batch, seq, channels, states, kernel_size, d=None, conv_state=None,
+                ssm_state=None):
+    """The stages of Mamba2Mixer::forward (mamba2.rs:264-375) between the five
+    input projections and out_proj, per batch: conv input = K-1 cached (or
+    zero) steps + x; depthwise conv; drop the prefix; SiLU; selective scan with
+    softplus(dt), delta_bias 0; gated RMSNorm per row of width C.
+
+    Inputs are [batch*seq, width] row-major (x/dt/gate width C, b/c width C*S).
+    Returns (normalised [batch*seq, C], new conv_state [batch, K-1, C],
+    final ssm_state [batch, C, S])."""
+    C, S, K, T = channels, states, kernel_size, seq
+    P = K - 1
+    xs = np.asarray(x_proj, np.float32).reshape(batch, T, C)
+    dts = np.asarray(delta_t, np.float32).reshape(batch, T, C)
+    bs = np.asarray(b, np.float32).reshape(batch, T * C * S)
+    cs = np.asarray(c, np.float32).reshape(batch, T * C * S)
+    gs = np.asarray(gate, np.float32).reshape(batch, T, C)
+    out = np.zeros((batch, T, C), np.float32)
+    new_conv = np.zeros((batch, P, C), np.float32)
+    fin = np.zeros((batch, C, S), np.float32)
+    for bi in range(batch):
+        prefix = (np.zeros((P, C), np.float32) if conv_state is None
+                  else np.asarray(conv_state, np.float32).reshape(batch, P, C)[bi])
+        conv_in = np.concatenate([prefix, xs[bi]], axis=0)
+        conv = conv1d(conv_in, conv_weights, T + P, C, K).reshape(T + P, C)[P:]
+        act = silu_array(conv)
+        init = None if ssm_state is None else np.asarray(ssm_state, np.float32).reshape(batch, -1)[bi]
+        vals, f = selective_scan(act, dts[bi], ssm_a, bs[bi], cs[bi], T, C, S, d=d,
+                                 initial_state=init, delta_bias=0.0, softplus=True)
+        out[bi] = rms_norm_rows(vals, norm_weight, epsilon, C, gate=gs[bi]).reshape(T, C)
+        new_conv[bi] = conv_in[len(conv_in) - P:] if P else new_conv[bi]
+        fin[bi] = f.reshape(C, S)
+    return out.reshape(batch * T, C), new_conv, fin

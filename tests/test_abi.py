@@ -111,3 +111,37 @@ def test_moe_layer_validation():
     assert b.value > 0
     assert lib.nk_moe_forward(ctypes.byref(s), None, 4, None, nk.F32, None, None, None, 0,
                               None) == nk.WORKSPACE_TOO_SMALL
+
+
+def test_mamba_glue_validation_order():
+    lib = nk.lib()
+    # conv1d.rs:126-158: shape, then input, weights, output lengths
+    assert lib.nk_conv1d(None, 0, None, 0, 1, 0, 1, None, 0, None) == nk.INVALID_SHAPE
+    assert lib.nk_conv1d(None, 1, None, 2, 2, 1, 2, None, 2, None) == nk.LENGTH_MISMATCH
+    assert (err().argument, err().expected, err().actual) == (b"input", 2, 1)
+    assert lib.nk_conv1d(None, 2, None, 1, 2, 1, 2, None, 2, None) == nk.LENGTH_MISMATCH
+    assert err().argument == b"weights"
+    assert lib.nk_conv1d(None, 2, None, 2, 2, 1, 2, None, 1, None) == nk.LENGTH_MISMATCH
+    assert err().argument == b"output"
+    # ssm.rs:177-245: shape (seq 0 is invalid here), then input .. final_state
+    z = [None, 0]
+    assert lib.nk_selective_scan(*z * 7, 0.0, 0, 0, 1, 1, None, 0, None, 1, None) \
+        == nk.INVALID_SHAPE
+    lens = [1, 1, 1, 0, 1]  # b is short
+    args = []
+    for n in lens:
+        args += [None, n]
+    args += [None, 0, None, 0]  # d, initial_state absent
+    assert lib.nk_selective_scan(*args, 0.0, 0, 1, 1, 1, None, 1, None, 1, None) \
+        == nk.LENGTH_MISMATCH
+    assert (err().argument, err().expected, err().actual) == (b"b", 1, 0)
+    # rms_norm.rs:146-183 then :108-115: empty, weight, gate, output, epsilon
+    assert lib.nk_rms_norm(None, 0, None, 0, None, 0, 1e-5, None, 0, None) == nk.EMPTY_INPUT
+    assert lib.nk_rms_norm(None, 2, None, 1, None, 0, 1e-5, None, 2, None) == nk.LENGTH_MISMATCH
+    assert (err().argument, err().expected, err().actual) == (b"weight", 2, 1)
+    g = ctypes.c_void_p(16)  # non-NULL gate: only its length is read
+    assert lib.nk_rms_norm(None, 2, None, 2, g, 1, 1e-5, None, 2, None) == nk.LENGTH_MISMATCH
+    assert err().argument == b"gate"
+    assert lib.nk_rms_norm(None, 2, None, 2, None, 0, -1.0, None, 2, None) \
+        == nk.NEGATIVE_EPSILON
+    assert err().value == -1.0
