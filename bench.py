@@ -278,10 +278,81 @@ def tp_projections(torch, dev, world, reps=10):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
     flops = 2 * T_ * HM * NIN + 2 * T_ * KOUT * HM
-    return {"config": "Mamba2 in_proj 4096->18560 (column-parallel) + out_proj 8192->4096 "
-                      "(row-parallel, NCCL all-reduce), T=8192 bf16",
-            "ms": round(ms, 4), "tflops_total": round(flops / ms / 1e9, 1),
-            "tflops_per_gpu": round(flops / ms / 1e9 / world, 1), "n_gpus": world}
+    res = {"config": "Mamba2 in_proj 4096->18560 (column-parallel) + out_proj 8192->4096 "
+                     "(row-parallel, NCCL all-reduce), T=8192 bf16",
+           "ms": round(ms, 4), "tflops_total": round(flops / ms / 1e9, 1),
+           "tflops_per_gpu": round(flops / ms / 1e9 / world, 1), "n_gpus": world}
+    res["block"] = mamba_block(torch, dev, world, w_in, w_out, x, reps)
+    return res
+
+
+def mamba_block(torch, dev, world, w_in, w_out, x, reps):
+    """The whole config-4 Mamba2 block: in_proj GEMM -> causal conv + SiLU ->
+    selective scan (d_state 128, 128 heads x 64, 8 groups) -> gated RMSNorm ->
+    out_proj GEMM (+ the norm's and the output's all-reduces under TP).
+    Stage times come from CUDA events on the launching stream."""
+    import torch.distributed as dist
+
+    import nk
+    import nk_mamba
+
+    H, P, G, S, K = 128, 64, 8, 128, 4
+    C = H * P
+    g = torch.Generator(device=dev).manual_seed(11)
+    conv = torch.randn(C, K, device=dev, generator=g) * 0.5
+    a = -torch.rand(H, device=dev, generator=g) - 0.5
+    d = torch.randn(H, device=dev, generator=g)
+    nw = torch.randn(C, device=dev, generator=g)
+    blk = nk_mamba.Mamba2Block(w_in, w_out, conv, a, d, nw, heads=H, head_dim=P, groups=G,
+                               state=S, kernel_size=K)
+    T_ = x.shape[0]
+    for _ in range(3):
+        blk.forward(x, 1, T_)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for _ in range(reps):
+        blk.forward(x, 1, T_)
+    e_.record()
+    e_.synchronize()
+    ms = s_.elapsed_time(e_) / reps
+    # one more pass with events between the stages (same kernels, same stream)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    C_l, W = blk.C, blk.width
+    evs[0].record()
+    fused = nk.gemm(x, blk.w_in, out_dtype=torch.float32)
+    evs[1].record()
+    act = nk.conv1d_ex(fused[:, C_l:2 * C_l], blk.conv_w, 1, T_, C_l, K, ld_x=W, silu=True,
+                       f32_accumulate=True)
+    y = torch.empty(T_, C_l, device=dev)
+    fin = torch.empty(1, C_l, S, device=dev)
+    base = fused.data_ptr()
+    args = nk.NkScanArgs(1, T_, C_l, S, act.data_ptr(), C_l,
+                         base + 4 * (2 * C_l + 2 * blk.G * S), W, P, blk.a.data_ptr(), P, 0,
+                         base + 4 * 2 * C_l, base + 4 * (2 * C_l + blk.G * S), W, blk.bc_group,
+                         blk.d.data_ptr(), P, None, 0.0, 1, y.data_ptr(), C_l, fin.data_ptr(), 0)
+    evs[2].record()
+    nk.selective_scan_ex(args)
+    evs[3].record()
+    normed = nk.rms_norm_rows(y, blk.norm_w, 1e-5, gate=fused[:, :C_l], out_dtype=nk.BF16)
+    nk.gemm(normed, blk.w_out, out_dtype=torch.float32)
+    evs[4].record()
+    evs[4].synchronize()
+    stages = {"in_proj": evs[0].elapsed_time(evs[1]), "conv_silu": evs[1].elapsed_time(evs[2]),
+              "scan": evs[2].elapsed_time(evs[3]), "norm_out_proj": evs[3].elapsed_time(evs[4])}
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    scan_updates = T_ * C_l * S
+    return {"config": "Mamba2 block (in_proj, conv+SiLU, selective scan d_state 128, gated "
+                      "RMSNorm, out_proj), T=8192, hidden 4096, 128 heads x 64, 8 groups",
+            "ms": round(ms, 4), "tokens_per_s": round(T_ / (ms / 1e3)),
+            "stages_ms_rank0": {k: round(v, 4) for k, v in stages.items()},
+            "scan_state_updates_per_s": round(scan_updates / (stages["scan"] / 1e3) / 1e9, 1),
+            "scan_unit": "G state updates/s (per GPU)", "n_gpus": world}
 
 
 class EpTimer:

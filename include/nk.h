@@ -459,6 +459,19 @@ nk_status nk_rms_norm_rows(const float *x, int64_t rows, int64_t width, int64_t 
                            int64_t ld_gate, float epsilon, void *out, int64_t ld_out,
                            int32_t out_dtype, void *stream);
 
+/* The same norm with each row split over tensor-parallel ranks (a rank holds
+ * `width` of the row's `total_width` columns): nk_row_sumsq writes each local
+ * row's f64 sum of squares, the caller sums them over the ranks (one
+ * all-reduce of `rows` doubles), and nk_rms_norm_rows_presummed normalises
+ * the local columns with the full-row mean square sumsq[row] / total_width. */
+nk_status nk_row_sumsq(const float *x, int64_t rows, int64_t width, int64_t ld_x, double *sumsq,
+                       void *stream);
+nk_status nk_rms_norm_rows_presummed(const float *x, int64_t rows, int64_t width, int64_t ld_x,
+                                     const float *weight, size_t weight_len, const float *gate,
+                                     int64_t ld_gate, const double *sumsq, int64_t total_width,
+                                     float epsilon, void *out, int64_t ld_out,
+                                     int32_t out_dtype, void *stream);
+
 #pragma GCC visibility pop
 #endif
 

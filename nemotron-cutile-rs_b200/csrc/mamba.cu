@@ -523,29 +523,46 @@ __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(Sca
 }
 
 // ---------------------------------------------------------------------- norm
+// Block-wide f64 sum over 256 threads (result valid in every thread).
+__device__ __forceinline__ double block_sum_256(double v) {
+  __shared__ double part[8];
+  __shared__ double total;
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < 8; ++i) t += part[i];
+    total = t;
+  }
+  __syncthreads();
+  return total;
+}
+
+// presum == NULL: the row's own f64 sum of squares over W; else presum[row]
+// is the sum over the full row of total_w elements (the row split over
+// tensor-parallel ranks, summed by an all-reduce).
 template <bool GATE, bool BF16>
 __global__ void __launch_bounds__(256) rms_rows_kernel(const float *__restrict__ x, int64_t ld_x,
                                                        const float *__restrict__ w,
                                                        const float *__restrict__ g,
                                                        int64_t ld_g, int64_t W, float eps,
-                                                       void *__restrict__ out, int64_t ld_out) {
+                                                       const double *__restrict__ presum,
+                                                       int64_t total_w, void *__restrict__ out,
+                                                       int64_t ld_out) {
   const int64_t row = blockIdx.x;
   const float *xr = x + row * ld_x;
-  double sum = 0.0;
-  for (int64_t i = threadIdx.x; i < W; i += blockDim.x) sum += (double)xr[i] * (double)xr[i];
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  __shared__ double part[8];
-  __shared__ float scale_s;
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double tot = 0.0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += part[i];
-    const float denom = sqrtf((float)(tot / (double)W) + eps);  // rms_norm.rs:117-123
-    scale_s = 1.0f / denom;
+  double tot;
+  if (presum) {
+    tot = presum[row];
+  } else {
+    double sum = 0.0;
+    for (int64_t i = threadIdx.x; i < W; i += blockDim.x) sum += (double)xr[i] * (double)xr[i];
+    tot = block_sum_256(sum);
   }
-  __syncthreads();
-  const float scale = scale_s;
+  // rms_norm.rs:117-123: mean square in f64, cast to f32, + eps, sqrt, reciprocal.
+  const float denom = sqrtf((float)(tot / (double)total_w) + eps);
+  const float scale = 1.0f / denom;
   for (int64_t i = threadIdx.x; i < W; i += blockDim.x) {
     float v = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
     if (GATE) v = __fmul_rn(v, g[row * ld_g + i]);
@@ -554,6 +571,15 @@ __global__ void __launch_bounds__(256) rms_rows_kernel(const float *__restrict__
     else
       reinterpret_cast<float *>(out)[row * ld_out + i] = v;
   }
+}
+
+__global__ void __launch_bounds__(256) row_sumsq_kernel(const float *__restrict__ x, int64_t ld_x,
+                                                        int64_t W, double *__restrict__ out) {
+  const float *xr = x + (int64_t)blockIdx.x * ld_x;
+  double sum = 0.0;
+  for (int64_t i = threadIdx.x; i < W; i += blockDim.x) sum += (double)xr[i] * (double)xr[i];
+  sum = block_sum_256(sum);
+  if (threadIdx.x == 0) out[blockIdx.x] = sum;
 }
 
 // ---------------------------------------------------------------- launchers
@@ -710,17 +736,15 @@ static nk_status launch_scan(const nk_scan_args &a, cudaStream_t s) {
 
 static nk_status launch_rms_rows(const float *x, int64_t rows, int64_t width, int64_t ld_x,
                                  const float *w, const float *g, int64_t ld_g, float eps,
-                                 void *out, int64_t ld_out, int out_dtype, cudaStream_t s) {
+                                 const double *presum, int64_t total_w, void *out,
+                                 int64_t ld_out, int out_dtype, cudaStream_t s) {
   if (rows == 0) return ok();
+  if (rows > 0x7fffffff) return fail(NK_UNSUPPORTED, "rms norm rows < 2^31");
   const bool bf = out_dtype == NK_DTYPE_BF16;
   const dim3 grid((unsigned)rows);
-  if (g) {
-    if (bf) rms_rows_kernel<true, true><<<grid, 256, 0, s>>>(x, ld_x, w, g, ld_g, width, eps, out, ld_out);
-    else rms_rows_kernel<true, false><<<grid, 256, 0, s>>>(x, ld_x, w, g, ld_g, width, eps, out, ld_out);
-  } else {
-    if (bf) rms_rows_kernel<false, true><<<grid, 256, 0, s>>>(x, ld_x, w, g, ld_g, width, eps, out, ld_out);
-    else rms_rows_kernel<false, false><<<grid, 256, 0, s>>>(x, ld_x, w, g, ld_g, width, eps, out, ld_out);
-  }
+  auto kern = g ? (bf ? rms_rows_kernel<true, true> : rms_rows_kernel<true, false>)
+                : (bf ? rms_rows_kernel<false, true> : rms_rows_kernel<false, false>);
+  kern<<<grid, 256, 0, s>>>(x, ld_x, w, g, ld_g, width, eps, presum, total_w, out, ld_out);
   return check_launch("rms_rows_kernel");
 }
 
@@ -818,7 +842,8 @@ nk_status nk_rms_norm(const float *input, size_t len, const float *weight, size_
   if (out_len != len) return fail_length("output", len, out_len);
   if (epsilon < 0.0f) return fail_eps(epsilon);
   return launch_rms_rows(input, 1, (int64_t)len, (int64_t)len, weight, gate, (int64_t)len,
-                         epsilon, out, (int64_t)len, NK_DTYPE_F32, as_stream(stream));
+                         epsilon, nullptr, (int64_t)len, out, (int64_t)len, NK_DTYPE_F32,
+                         as_stream(stream));
 }
 
 nk_status nk_rms_norm_rows(const float *x, int64_t rows, int64_t width, int64_t ld_x,
@@ -834,8 +859,35 @@ nk_status nk_rms_norm_rows(const float *x, int64_t rows, int64_t width, int64_t 
     return fail(NK_INVALID_PARAMS, "row strides must be >= width");
   if (out_dtype != NK_DTYPE_F32 && out_dtype != NK_DTYPE_BF16)
     return fail(NK_INVALID_PARAMS, "out_dtype must be NK_DTYPE_F32 or NK_DTYPE_BF16");
-  return launch_rms_rows(x, rows, width, ld_x, weight, gate, ld_gate, epsilon, out, ld_out,
-                         out_dtype, as_stream(stream));
+  return launch_rms_rows(x, rows, width, ld_x, weight, gate, ld_gate, epsilon, nullptr, width,
+                         out, ld_out, out_dtype, as_stream(stream));
+}
+
+nk_status nk_row_sumsq(const float *x, int64_t rows, int64_t width, int64_t ld_x, double *sumsq,
+                       void *stream) {
+  if (rows < 0 || width <= 0 || ld_x < width) return fail(NK_INVALID_SHAPE, "rows >= 0, 0 < width <= ld_x");
+  if (rows == 0) return ok();
+  if (rows > 0x7fffffff) return fail(NK_UNSUPPORTED, "rows < 2^31");
+  row_sumsq_kernel<<<(unsigned)rows, 256, 0, as_stream(stream)>>>(x, ld_x, width, sumsq);
+  return check_launch("row_sumsq_kernel");
+}
+
+nk_status nk_rms_norm_rows_presummed(const float *x, int64_t rows, int64_t width, int64_t ld_x,
+                                     const float *weight, size_t weight_len, const float *gate,
+                                     int64_t ld_gate, const double *sumsq, int64_t total_width,
+                                     float epsilon, void *out, int64_t ld_out,
+                                     int32_t out_dtype, void *stream) {
+  if (rows < 0 || width <= 0 || total_width < width)
+    return fail(NK_INVALID_SHAPE, "rows >= 0, 0 < width <= total_width");
+  if (epsilon < 0.0f) return fail_eps(epsilon);
+  if (weight_len != (uint64_t)width) return fail_length("weight", width, weight_len);
+  if (!sumsq) return fail(NK_INVALID_PARAMS, "sumsq is required");
+  if (ld_x < width || ld_out < width || (gate && ld_gate < width))
+    return fail(NK_INVALID_PARAMS, "row strides must be >= width");
+  if (out_dtype != NK_DTYPE_F32 && out_dtype != NK_DTYPE_BF16)
+    return fail(NK_INVALID_PARAMS, "out_dtype must be NK_DTYPE_F32 or NK_DTYPE_BF16");
+  return launch_rms_rows(x, rows, width, ld_x, weight, gate, ld_gate, epsilon, sumsq,
+                         total_width, out, ld_out, out_dtype, as_stream(stream));
 }
 
 }  // extern "C"

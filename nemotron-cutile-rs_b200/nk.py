@@ -149,6 +149,9 @@ _SIGS = {
     "nk_rms_norm": (_i32, [_p, _sz, _p, _sz, _p, _sz, _f, _p, _sz, _p]),
     "nk_rms_norm_rows": (_i32, [_p, _i64, _i64, _i64, _p, _sz, _p, _i64, _f, _p, _i64, _i32,
                                 _p]),
+    "nk_row_sumsq": (_i32, [_p, _i64, _i64, _i64, _p, _p]),
+    "nk_rms_norm_rows_presummed": (_i32, [_p, _i64, _i64, _i64, _p, _sz, _p, _i64, _p, _i64,
+                                          _f, _p, _i64, _i32, _p]),
     "nk_set_stage_timing": (_i32, [_i32]),
     "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }
@@ -481,4 +484,33 @@ def rms_norm_rows(x, weight, epsilon: float, gate=None, out_dtype: int = F32, ou
     call("nk_rms_norm_rows", ptr(x), rows, width, x.stride(0), ptr(weight), weight.numel(),
          ptr(gate), gate.stride(0) if gate is not None else 0, epsilon, ptr(out),
          out.stride(0), out_dtype, stream_ptr(stream))
+    return out
+
+
+def row_sumsq(x, out=None, stream=None):
+    """f64 sum of squares of each row of x [rows, width] (nk_row_sumsq)."""
+    import torch
+
+    _require_cuda(x, out)
+    rows, width = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float64, device=x.device)
+    call("nk_row_sumsq", ptr(x), rows, width, x.stride(0), ptr(out), stream_ptr(stream))
+    return out
+
+
+def rms_norm_rows_presummed(x, weight, epsilon: float, sumsq, total_width: int, gate=None,
+                            out_dtype: int = F32, out=None, stream=None):
+    """Row-wise (gated) RMSNorm of the local columns of rows split over ranks;
+    sumsq [rows] f64 holds the full rows' sums of squares."""
+    import torch
+
+    _require_cuda(x, weight, gate, sumsq, out)
+    rows, width = x.shape
+    if out is None:
+        out = torch.empty(rows, width, device=x.device,
+                          dtype=torch.bfloat16 if out_dtype == BF16 else torch.float32)
+    call("nk_rms_norm_rows_presummed", ptr(x), rows, width, x.stride(0), ptr(weight),
+         weight.numel(), ptr(gate), gate.stride(0) if gate is not None else 0, ptr(sumsq),
+         total_width, epsilon, ptr(out), out.stride(0), out_dtype, stream_ptr(stream))
     return out
