@@ -107,13 +107,23 @@ __global__ void proj_simt_kernel(const void *__restrict__ x, int x_f32,
 }
 
 // y[m, n] = act(Σ_s partial[s][m, n] + bias[n]), partial sums added in split order.
+// Launched as a programmatic dependent of the GEMM: its blocks are scheduled
+// while the GEMM runs and wait (griddepcontrol.wait) for its completion, so the
+// launch latency is hidden.  Loads of four splits are issued together.
 __global__ void splitk_reduce_kernel(const float *__restrict__ part, int splits, int64_t mn,
                                      int64_t n, const float *__restrict__ bias, int relu2,
                                      void *__restrict__ y, int y_f32) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= mn) return;
   float acc = part[i];
-  for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[(int64_t)s * mn + i]);
+  int s = 1;
+  for (; s + 4 <= splits; s += 4) {
+    const float a0 = part[(int64_t)s * mn + i], a1 = part[(int64_t)(s + 1) * mn + i];
+    const float a2 = part[(int64_t)(s + 2) * mn + i], a3 = part[(int64_t)(s + 3) * mn + i];
+    acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, a0), a1), a2), a3);
+  }
+  for (; s < splits; ++s) acc = __fadd_rn(acc, part[(int64_t)s * mn + i]);
   if (bias) acc = __fadd_rn(acc, bias[i % n]);
   if (relu2) acc = nk_relu2(acc);
   if (y_f32)
@@ -272,9 +282,18 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
   nk_status st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream, pair);
   if (st != NK_OK || splits == 1) return st;
   const int64_t mn = m * n;
-  splitk_reduce_kernel<<<(unsigned)ceil_div(mn, 256), 256, 0, stream>>>(
-      reinterpret_cast<const float *>(buf + part_off), splits, mn, n, bias, relu2, y,
-      y_dtype == NK_F32);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ceil_div(mn, 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NK_CUDA_TRY(cudaLaunchKernelEx(&cfg, splitk_reduce_kernel,
+                                 reinterpret_cast<const float *>(buf + part_off), splits, mn,
+                                 n, bias, (int)relu2, y, (int)(y_dtype == NK_F32)));
   return check_launch("splitk_reduce_kernel");
 }
 

@@ -108,6 +108,12 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
   if (PAIR == 2) cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the next kernel on the stream may be
+  // scheduled from here on (it waits for this grid to complete before it
+  // touches memory), and this grid's first global read waits for the
+  // previous kernel's results.  The setup above overlapped its tail.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // shared::cluster addresses of the leader's barriers (PAIR == 2)
   auto leader_bar = [&](uint64_t *b) -> uint32_t { return mapa_cta(smem_u32(b), 0); };
@@ -463,24 +469,22 @@ nk_status launch_impl(const CUtensorMap &wm, const CUtensorMap &xm, const TcArgs
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(tc_gemm)");
     attr_done = true;
   }
-  if (PAIR == 1) {
-    tc_gemm_kernel<WK, BN, 1><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(wm, xm, args);
-    return check_launch("tc_gemm_kernel");
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(Cfg::kThreads);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = PAIR == 2 ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WK, BN, PAIR>, wm, xm, args);
-  if (e != cudaSuccess) return fail_cuda(e, "cudaLaunchKernelEx(tc_gemm pair)");
+  if (e != cudaSuccess) return fail_cuda(e, "cudaLaunchKernelEx(tc_gemm)");
   return check_launch("tc_gemm_kernel pair");
 }
 
