@@ -108,11 +108,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
   if (PAIR == 2) cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Programmatic dependent launch: the next kernel on the stream may be
-  // scheduled from here on (it waits for this grid to complete before it
-  // touches memory), and this grid's first global read waits for the
-  // previous kernel's results.  The setup above overlapped its tail.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Programmatic dependent launch: this grid's first global read waits for
+  // the previous kernel's results; the setup above overlapped its tail.
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // shared::cluster addresses of the leader's barriers (PAIR == 2)
@@ -394,6 +391,11 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // This CTA's work is done: the next kernel on the stream may be scheduled
+  // (it still waits for this grid to complete before touching memory).
+  // Triggering only now keeps early dependents from occupying SMs that a
+  // concurrent stream (the shared expert) is meant to use.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (PAIR == 2) {
     if (*abort_v) {  // let any copy still in flight from this CTA land (bounded)
       const uint64_t t0 = nk_globaltimer();

@@ -15,7 +15,7 @@ import os
 from dataclasses import dataclass
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libnk.so")
+LIB_PATH = os.environ.get("NK_LIB_PATH") or os.path.join(_HERE, "libnk.so")
 
 # status codes (nk.h)
 OK, INVALID_SHAPE, LENGTH_MISMATCH, INVALID_PARAMS, INT4_OUT_OF_RANGE = 0, 1, 2, 3, 4
