@@ -52,7 +52,11 @@ enum {
   NK_WORKSPACE_TOO_SMALL = 10,
   NK_INVALID_DELTA_T = 11,   /* SsmError::InvalidDeltaT (index = (b*seq + t)*C + ch, value = dt) */
   NK_EMPTY_INPUT = 12,       /* RmsNormError::EmptyInput */
-  NK_NEGATIVE_EPSILON = 13   /* RmsNormError::NegativeEpsilon (value = epsilon) */
+  NK_NEGATIVE_EPSILON = 13,  /* RmsNormError::NegativeEpsilon (value = epsilon) */
+  NK_HEAD_COUNT_MISMATCH = 14, /* AttentionError::HeadCountMismatch (expected = Hq, actual = Hkv) */
+  NK_INVALID_SCALE = 15,     /* AttentionError::InvalidScale (value = scale) */
+  NK_NO_VALID_TARGETS = 16,  /* AttentionError::NoValidAttentionTargets (index = (b*Sq + q)*Hq + h) */
+  NK_ZERO_PARTITION = 17     /* AttentionError::ZeroPartition (index as above) */
 };
 
 typedef struct nk_error_info {
@@ -471,6 +475,52 @@ nk_status nk_rms_norm_rows_presummed(const float *x, int64_t rows, int64_t width
                                      int64_t ld_gate, const double *sumsq, int64_t total_width,
                                      float epsilon, void *out, int64_t ld_out,
                                      int32_t out_dtype, void *stream);
+
+/* ===================================================== attention core ====
+ * nemotron-kernels/src/attention.rs; layouts [batch, seq, heads, head_dim]. */
+
+/* Replaces scaled_dot_product_attention_into_host / scaled_dot_product_attention
+ * (attention.rs:204-302, 849-884) on f32 device tensors: f64 dot products,
+ * f32 scale (default 1/sqrt(head_dim) when has_scale = 0), f32 exp with an
+ * f64 partition, f64 output sums.  causal masks keys beyond
+ * min(q_offset + q, kv_seq - 1).  Validation order and errors as
+ * attention.rs:304-357 then the output length then the scale; the row
+ * errors (NoValidAttentionTargets, ZeroPartition) report the first row in
+ * (batch, query, head) order.  Synchronises `stream`. */
+nk_status nk_attention_f32(const float *query, size_t query_len, const float *key,
+                           size_t key_len, const float *value, size_t value_len, int64_t batch,
+                           int64_t q_seq, int64_t kv_seq, int64_t q_heads, int64_t kv_heads,
+                           int64_t head_dim, int32_t causal, int64_t q_offset,
+                           int32_t has_scale, float scale, float *out, size_t out_len,
+                           void *stream);
+
+/* KV cache (the serving path's replacement for KvCache::append, cache.rs:74-110):
+ * k_cache bf16 [batch, kv_heads, max_len, head_dim], vt_cache bf16
+ * [batch, kv_heads, head_dim, max_len] (V stored transposed).  Writes steps
+ * pos0 .. pos0+seq-1 from the K/V projection outputs k_new / v_new
+ * [batch*seq, kv_heads*head_dim] bf16.  Allocate the caches zeroed: the
+ * value GEMM reads up to 63 positions past kv_len (multiplied by 0). */
+nk_status nk_kv_append(const uint16_t *k_new, const uint16_t *v_new, int64_t batch, int64_t seq,
+                       int64_t kv_heads, int64_t head_dim, int64_t pos0, int64_t max_len,
+                       uint16_t *k_cache, uint16_t *vt_cache, void *stream);
+
+/* Grouped-query attention of q bf16 [batch*q_seq, q_heads*head_dim] over the
+ * first kv_len cache positions: scores and value sums on the tcgen05 GEMM
+ * (bf16 operands, f32 accumulation), softmax as the reference (f32 exp, f64
+ * partition).  out [batch*q_seq, q_heads*head_dim], f32 or bf16 (out_dtype).
+ * head_dim 64 or 128, max_len a multiple of 64.  A row without a finite
+ * score is flagged in the workspace (nk_attention_check), not raised, so
+ * the call does not synchronise. */
+nk_status nk_attention_workspace_bytes(int64_t batch, int64_t q_seq, int64_t kv_len,
+                                       int64_t max_len, int64_t q_heads, int64_t kv_heads,
+                                       int64_t head_dim, size_t *bytes);
+nk_status nk_attention_gqa(const uint16_t *q, const uint16_t *k_cache, const uint16_t *vt_cache,
+                           int64_t batch, int64_t q_seq, int64_t kv_len, int64_t max_len,
+                           int64_t q_heads, int64_t kv_heads, int64_t head_dim, int32_t causal,
+                           int64_t q_offset, int32_t has_scale, float scale, void *out,
+                           int32_t out_dtype, void *workspace, size_t workspace_bytes,
+                           void *stream);
+nk_status nk_attention_check(const void *workspace, int64_t *first_bad_row, void *stream);
 
 #pragma GCC visibility pop
 #endif

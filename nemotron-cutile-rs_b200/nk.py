@@ -21,11 +21,13 @@ LIB_PATH = os.environ.get("NK_LIB_PATH") or os.path.join(_HERE, "libnk.so")
 OK, INVALID_SHAPE, LENGTH_MISMATCH, INVALID_PARAMS, INT4_OUT_OF_RANGE = 0, 1, 2, 3, 4
 NON_FINITE_INPUT, INVALID_ROW_COUNT, UNSUPPORTED, DEVICE_ERROR, TIMEOUT = 5, 6, 7, 8, 9
 WORKSPACE_TOO_SMALL, INVALID_DELTA_T, EMPTY_INPUT, NEGATIVE_EPSILON = 10, 11, 12, 13
+HEAD_COUNT_MISMATCH, INVALID_SCALE, NO_VALID_TARGETS, ZERO_PARTITION = 14, 15, 16, 17
 STATUS_NAMES = {
     0: "Ok", 1: "InvalidShape", 2: "LengthMismatch", 3: "InvalidParams",
     4: "Int4OutOfRange", 5: "NonFiniteInput", 6: "InvalidRowCount", 7: "Unsupported",
     8: "DeviceError", 9: "Timeout", 10: "WorkspaceTooSmall", 11: "InvalidDeltaT",
-    12: "EmptyInput", 13: "NegativeEpsilon",
+    12: "EmptyInput", 13: "NegativeEpsilon", 14: "HeadCountMismatch", 15: "InvalidScale",
+    16: "NoValidAttentionTargets", 17: "ZeroPartition",
 }
 F32, BF16 = 0, 1
 EPI_RELU2 = 1
@@ -152,6 +154,13 @@ _SIGS = {
     "nk_row_sumsq": (_i32, [_p, _i64, _i64, _i64, _p, _p]),
     "nk_rms_norm_rows_presummed": (_i32, [_p, _i64, _i64, _i64, _p, _sz, _p, _i64, _p, _i64,
                                           _f, _p, _i64, _i32, _p]),
+    "nk_attention_f32": (_i32, [_p, _sz, _p, _sz, _p, _sz, _i64, _i64, _i64, _i64, _i64, _i64,
+                                _i32, _i64, _i32, _f, _p, _sz, _p]),
+    "nk_kv_append": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "nk_attention_workspace_bytes": (_i32, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
+    "nk_attention_gqa": (_i32, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32,
+                                _i64, _i32, _f, _p, _i32, _p, _sz, _p]),
+    "nk_attention_check": (_i32, [_p, _p, _p]),
     "nk_set_stage_timing": (_i32, [_i32]),
     "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }
@@ -514,3 +523,77 @@ def rms_norm_rows_presummed(x, weight, epsilon: float, sumsq, total_width: int, 
          weight.numel(), ptr(gate), gate.stride(0) if gate is not None else 0, ptr(sumsq),
          total_width, epsilon, ptr(out), out.stride(0), out_dtype, stream_ptr(stream))
     return out
+
+
+# ------------------------------------------------------------ attention core
+def attention_f32(q, k, v, batch, q_seq, kv_seq, q_heads, kv_heads, head_dim, *, causal=False,
+                  q_offset=0, scale=None, out=None, stream=None):
+    """scaled_dot_product_attention (attention.rs:204-302) on f32 [B, S, H, d] device tensors."""
+    import torch
+
+    _require_cuda(q, k, v, out)
+    n = batch * q_seq * q_heads * head_dim
+    ol = n if out is None else out.numel()
+    if out is None:
+        out = torch.empty(max(n, 1), dtype=torch.float32, device=q.device)
+    call("nk_attention_f32", ptr(q), q.numel(), ptr(k), k.numel(), ptr(v), v.numel(), batch,
+         q_seq, kv_seq, q_heads, kv_heads, head_dim, 1 if causal else 0, q_offset,
+         0 if scale is None else 1, 0.0 if scale is None else scale, ptr(out), ol,
+         stream_ptr(stream))
+    return out[:ol]
+
+
+class KvCache:
+    """The serving KV cache: K [B, Hkv, max_len, d] and V transposed
+    [B, Hkv, d, max_len], bf16, zero-initialised (nk_kv_append)."""
+
+    def __init__(self, batch, kv_heads, head_dim, max_len, device="cuda"):
+        import torch
+
+        self.batch, self.kv_heads, self.head_dim, self.max_len = batch, kv_heads, head_dim, max_len
+        self.k = torch.zeros(batch, kv_heads, max_len, head_dim, dtype=torch.bfloat16,
+                             device=device)
+        self.vt = torch.zeros(batch, kv_heads, head_dim, max_len, dtype=torch.bfloat16,
+                              device=device)
+        self.length = 0
+
+    def append(self, k_new, v_new, seq, stream=None):
+        """k_new / v_new bf16 [batch*seq, kv_heads*head_dim] at positions length.. ."""
+        _require_cuda(k_new, v_new)
+        call("nk_kv_append", ptr(k_new), ptr(v_new), self.batch, seq, self.kv_heads,
+             self.head_dim, self.length, self.max_len, ptr(self.k), ptr(self.vt),
+             stream_ptr(stream))
+        self.length += seq
+
+
+def attention_gqa(q, cache: KvCache, q_seq, q_heads, *, causal=True, q_offset=None, scale=None,
+                  out_dtype=BF16, out=None, workspace=None, stream=None):
+    """Grouped-query attention of q bf16 [B*q_seq, q_heads*d] over the cache's
+    first `cache.length` positions (nk_attention_gqa).  q_offset defaults to
+    cache.length - q_seq (the queries are the last q_seq positions)."""
+    import torch
+
+    _require_cuda(q, out, workspace)
+    B, Hkv, d, L = cache.batch, cache.kv_heads, cache.head_dim, cache.length
+    if q_offset is None:
+        q_offset = L - q_seq
+    need = ctypes.c_size_t(0)
+    call("nk_attention_workspace_bytes", B, q_seq, L, cache.max_len, q_heads, Hkv, d,
+         ctypes.byref(need))
+    if workspace is None or workspace.numel() < need.value:
+        workspace = torch.empty(need.value, dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty(B * q_seq, q_heads * d, device=q.device,
+                          dtype=torch.float32 if out_dtype == F32 else torch.bfloat16)
+    call("nk_attention_gqa", ptr(q), ptr(cache.k), ptr(cache.vt), B, q_seq, L, cache.max_len,
+         q_heads, Hkv, d, 1 if causal else 0, q_offset, 0 if scale is None else 1,
+         0.0 if scale is None else scale, ptr(out), out_dtype, ptr(workspace),
+         workspace.numel(), stream_ptr(stream))
+    return out, workspace
+
+
+def attention_check(workspace, stream=None) -> int:
+    """First output row without a finite score in the last nk_attention_gqa, or -1."""
+    r = ctypes.c_int64(0)
+    call("nk_attention_check", ptr(workspace), ctypes.byref(r), stream_ptr(stream))
+    return r.value

@@ -582,3 +582,98 @@ int orc_rms_norm(const float *input, size_t len, const float *weight, size_t wei
 void orc_silu_in_place(float *values, size_t n) {
   for (size_t i = 0; i < n; ++i) values[i] = orc_silu(values[i]);
 }
+
+/* ----------------------------------------------------------- attention core */
+
+static size_t attn_off(size_t b, size_t s, size_t h, size_t d, size_t seq, size_t heads,
+                       size_t hd) {
+  return ((b * seq + s) * heads + h) * hd + d; /* attention.rs:450-460 */
+}
+
+/* attention.rs:204-302 */
+int orc_attention(const float *q, size_t q_len, const float *k, size_t k_len, const float *v,
+                  size_t v_len, size_t batch, size_t q_seq, size_t kv_seq, size_t q_heads,
+                  size_t kv_heads, size_t head_dim, int causal, size_t q_offset, int has_scale,
+                  float scale, float *out, size_t out_len, orc_error *err) {
+  if (!batch || !q_seq || !kv_seq || !q_heads || !kv_heads || !head_dim)
+    return set_err(err, ORC_INVALID_SHAPE);
+  if (q_heads % kv_heads) return set_err(err, ORC_HEAD_COUNT_MISMATCH);
+  const size_t ql = batch * q_seq * q_heads * head_dim, kl = batch * kv_seq * kv_heads * head_dim;
+  if (q_len != ql) return len_err(err, "query", ql, q_len);
+  if (k_len != kl) return len_err(err, "key", kl, k_len);
+  if (v_len != kl) return len_err(err, "value", kl, v_len);
+  if (out_len != ql) return len_err(err, "output", ql, out_len);
+  const float sc = has_scale ? scale : 1.0f / sqrtf((float)head_dim); /* :82-93 */
+  if (!isfinite(sc) || sc <= 0.0f) {
+    if (err) {
+      err->code = ORC_INVALID_SCALE;
+      err->value = sc;
+    }
+    return ORC_INVALID_SCALE;
+  }
+  const size_t group = q_heads / kv_heads;
+  float *scores = (float *)malloc(sizeof(float) * kv_seq);
+  float *weights = (float *)malloc(sizeof(float) * kv_seq);
+  int rc = ORC_OK;
+  for (size_t b = 0; b < batch && rc == ORC_OK; ++b)
+    for (size_t qi = 0; qi < q_seq && rc == ORC_OK; ++qi) {
+      size_t max_key = kv_seq - 1;
+      if (causal) {
+        const size_t lim = q_offset + qi;
+        max_key = lim < kv_seq - 1 ? lim : kv_seq - 1;
+      }
+      for (size_t h = 0; h < q_heads && rc == ORC_OK; ++h) {
+        const size_t kh = h / group;
+        for (size_t j = 0; j < kv_seq; ++j) {
+          scores[j] = -INFINITY;
+          if (causal && j > max_key) continue;
+          double s = 0.0;
+          for (size_t d = 0; d < head_dim; ++d)
+            s += (double)q[attn_off(b, qi, h, d, q_seq, q_heads, head_dim)] *
+                 (double)k[attn_off(b, j, kh, d, kv_seq, kv_heads, head_dim)];
+          scores[j] = (float)s * sc;
+        }
+        float mx = -INFINITY;
+        for (size_t j = 0; j < kv_seq; ++j)
+          if (isfinite(scores[j])) mx = fmaxf(mx, scores[j]);
+        if (!isfinite(mx)) {
+          if (err) {
+            err->code = ORC_NO_VALID_TARGETS;
+            err->index = (b * q_seq + qi) * q_heads + h;
+          }
+          rc = ORC_NO_VALID_TARGETS;
+          break;
+        }
+        double part = 0.0;
+        for (size_t j = 0; j < kv_seq; ++j) {
+          if (isfinite(scores[j])) {
+            weights[j] = expf(scores[j] - mx);
+            part += (double)weights[j];
+          } else {
+            weights[j] = 0.0f;
+          }
+        }
+        if (part == 0.0) {
+          if (err) {
+            err->code = ORC_ZERO_PARTITION;
+            err->index = (b * q_seq + qi) * q_heads + h;
+          }
+          rc = ORC_ZERO_PARTITION;
+          break;
+        }
+        const float inv = (float)(1.0 / part);
+        for (size_t d = 0; d < head_dim; ++d) {
+          double acc = 0.0;
+          for (size_t j = 0; j < kv_seq; ++j) {
+            if (weights[j] == 0.0f) continue;
+            acc += (double)(weights[j] * inv) *
+                   (double)v[attn_off(b, j, kh, d, kv_seq, kv_heads, head_dim)];
+          }
+          out[attn_off(b, qi, h, d, q_seq, q_heads, head_dim)] = (float)acc;
+        }
+      }
+    }
+  free(scores);
+  free(weights);
+  return rc == ORC_OK ? set_err(err, ORC_OK) : rc;
+}

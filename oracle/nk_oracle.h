@@ -40,6 +40,10 @@ enum {
   ORC_INVALID_DELTA_T = 11,  /* ssm.rs SsmError::InvalidDeltaT; index = t*C + ch */
   ORC_EMPTY_INPUT = 12,      /* rms_norm.rs RmsNormError::EmptyInput */
   ORC_NEGATIVE_EPSILON = 13, /* rms_norm.rs RmsNormError::NegativeEpsilon; value = eps */
+  ORC_HEAD_COUNT_MISMATCH = 14, /* attention.rs HeadCountMismatch / InvalidHeadGrouping */
+  ORC_INVALID_SCALE = 15,       /* attention.rs InvalidScale; value = scale */
+  ORC_NO_VALID_TARGETS = 16,    /* attention.rs NoValidAttentionTargets; index = (b*Sq+q)*Hq+h */
+  ORC_ZERO_PARTITION = 17,      /* attention.rs ZeroPartition; index as above */
 };
 
 typedef struct orc_error {
@@ -157,6 +161,18 @@ int orc_selective_scan(const float *input, size_t input_len, const float *delta_
 int orc_rms_norm(const float *input, size_t len, const float *weight, size_t weight_len,
                  const float *gate, size_t gate_len, float epsilon, float *out, size_t out_len,
                  orc_error *err);
+
+/* ---- attention core (nemotron-kernels/src/attention.rs) ---- */
+
+/* scaled_dot_product_attention_into_host (attention.rs:204-302) with
+ * attention_scores_host (:132-190), validate_shape (:304-357) and
+ * AttentionOptions::resolve_scale (:82-93).  q [B, Sq, Hq, d], k/v
+ * [B, Skv, Hkv, d], out [B, Sq, Hq, d].  scale <= 0 with has_scale = 0 means
+ * the default 1/sqrt(d). */
+int orc_attention(const float *q, size_t q_len, const float *k, size_t k_len, const float *v,
+                  size_t v_len, size_t batch, size_t q_seq, size_t kv_seq, size_t q_heads,
+                  size_t kv_heads, size_t head_dim, int causal, size_t q_offset, int has_scale,
+                  float scale, float *out, size_t out_len, orc_error *err);
 
 /* bf16 helpers shared by the tests: round-to-nearest-even f32 -> bf16. */
 uint16_t orc_f32_to_bf16(float x);

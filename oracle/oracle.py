@@ -356,3 +356,28 @@ def mamba2_glue(x_proj, delta_t, b, c, gate, conv_weights, ssm_a, norm_weight, e
         new_conv[bi] = conv_in[len(conv_in) - P:] if P else new_conv[bi]
         fin[bi] = f.reshape(C, S)
     return out.reshape(batch * T, C), new_conv, fin
+
+
+# ------------------------------------------------------------ attention core
+
+ERR_NAMES.update({14: "HeadCountMismatch", 15: "InvalidScale", 16: "NoValidAttentionTargets",
+                  17: "ZeroPartition"})
+
+
+def attention(q, k, v, batch, q_seq, kv_seq, q_heads, kv_heads, head_dim, causal=False,
+              q_offset=0, scale=None, out_len=None):
+    """scaled_dot_product_attention_into_host (attention.rs:204-302); [B, S, H, d] layouts."""
+    (qa, qn), (ka, kn), (va, vn) = _arr(q), _arr(k), _arr(v)
+    ol = batch * q_seq * q_heads * head_dim if out_len is None else out_len
+    out = np.zeros(max(ol, 1), np.float32)
+    err = OrcError()
+    rc = lib().orc_attention(_p(qa), ctypes.c_size_t(qn), _p(ka), ctypes.c_size_t(kn), _p(va),
+                             ctypes.c_size_t(vn), ctypes.c_size_t(batch), ctypes.c_size_t(q_seq),
+                             ctypes.c_size_t(kv_seq), ctypes.c_size_t(q_heads),
+                             ctypes.c_size_t(kv_heads), ctypes.c_size_t(head_dim),
+                             ctypes.c_int(int(causal)), ctypes.c_size_t(q_offset),
+                             ctypes.c_int(0 if scale is None else 1),
+                             ctypes.c_float(0.0 if scale is None else scale), _p(out),
+                             ctypes.c_size_t(ol), ctypes.byref(err))
+    _check(rc, err)
+    return out[:ol]
