@@ -56,7 +56,8 @@ enum {
   NK_HEAD_COUNT_MISMATCH = 14, /* AttentionError::HeadCountMismatch (expected = Hq, actual = Hkv) */
   NK_INVALID_SCALE = 15,     /* AttentionError::InvalidScale (value = scale) */
   NK_NO_VALID_TARGETS = 16,  /* AttentionError::NoValidAttentionTargets (index = (b*Sq + q)*Hq + h) */
-  NK_ZERO_PARTITION = 17     /* AttentionError::ZeroPartition (index as above) */
+  NK_ZERO_PARTITION = 17,    /* AttentionError::ZeroPartition (index as above) */
+  NK_TOKEN_OUT_OF_RANGE = 18 /* EmbeddingError::TokenOutOfRange (actual = token id, expected = vocab, index = position) */
 };
 
 typedef struct nk_error_info {
@@ -521,6 +522,37 @@ nk_status nk_attention_gqa(const uint16_t *q, const uint16_t *k_cache, const uin
                            int32_t out_dtype, void *workspace, size_t workspace_bytes,
                            void *stream);
 nk_status nk_attention_check(const void *workspace, int64_t *first_bad_row, void *stream);
+
+/* ============================================ decoder steps around projections ====
+ * Embedding gather, block residual + RMSNorm, greedy pick. */
+
+/* Replaces embedding_lookup_into_host / embedding_lookup (nemotron-kernels/src/
+ * embedding.rs:73-91, 121-191): out[t] = table[token_ids[t]].  table
+ * [vocab_size, hidden_size] and out f32 or bf16 (NK_DTYPE_*).  Validation
+ * order: InvalidShape, LengthMismatch table / output, then TokenOutOfRange
+ * for the first bad id when check = 1 (which synchronises `stream`; with
+ * check = 0 bad ids leave their rows unwritten). */
+nk_status nk_embedding_lookup(const void *table, int32_t table_dtype, size_t table_len,
+                              const int32_t *token_ids, int64_t n_tokens, int64_t vocab_size,
+                              int64_t hidden_size, void *out, int32_t out_dtype, size_t out_len,
+                              int32_t check, void *stream);
+
+/* The residual of NemotronBlock::forward_into (nemotron-nn/src/block.rs:145-151)
+ * fused with the next RMSNorm (rms_norm.rs:117-123, the next block's input
+ * norm or the final norm, model.rs:296-301): per row of width,
+ * h_out = residual + delta (f32; delta NULL: h_out = residual; h_out may be
+ * residual) and normed = h_out * (1/sqrt(mean(h_out²) + epsilon)) * weight,
+ * f32 or bf16 (normed_dtype). */
+nk_status nk_add_rms_norm_rows(const float *residual, const float *delta, int64_t rows,
+                               int64_t width, const float *weight, size_t weight_len,
+                               float epsilon, float *h_out, void *normed, int32_t normed_dtype,
+                               void *stream);
+
+/* Greedy pick of predict_next_token (nemotron-model/src/model.rs:325-337) per
+ * row of x [rows, n] (row pitch ld, f32 or bf16): the index of the maximum
+ * under f32::total_cmp, the last one among equal maxima (Iterator::max_by). */
+nk_status nk_argmax_rows(const void *x, int32_t x_dtype, int64_t rows, int64_t n, int64_t ld,
+                         int32_t *out, void *stream);
 
 #pragma GCC visibility pop
 #endif

@@ -22,12 +22,13 @@ OK, INVALID_SHAPE, LENGTH_MISMATCH, INVALID_PARAMS, INT4_OUT_OF_RANGE = 0, 1, 2,
 NON_FINITE_INPUT, INVALID_ROW_COUNT, UNSUPPORTED, DEVICE_ERROR, TIMEOUT = 5, 6, 7, 8, 9
 WORKSPACE_TOO_SMALL, INVALID_DELTA_T, EMPTY_INPUT, NEGATIVE_EPSILON = 10, 11, 12, 13
 HEAD_COUNT_MISMATCH, INVALID_SCALE, NO_VALID_TARGETS, ZERO_PARTITION = 14, 15, 16, 17
+TOKEN_OUT_OF_RANGE = 18
 STATUS_NAMES = {
     0: "Ok", 1: "InvalidShape", 2: "LengthMismatch", 3: "InvalidParams",
     4: "Int4OutOfRange", 5: "NonFiniteInput", 6: "InvalidRowCount", 7: "Unsupported",
     8: "DeviceError", 9: "Timeout", 10: "WorkspaceTooSmall", 11: "InvalidDeltaT",
     12: "EmptyInput", 13: "NegativeEpsilon", 14: "HeadCountMismatch", 15: "InvalidScale",
-    16: "NoValidAttentionTargets", 17: "ZeroPartition",
+    16: "NoValidAttentionTargets", 17: "ZeroPartition", 18: "TokenOutOfRange",
 }
 F32, BF16 = 0, 1
 EPI_RELU2 = 1
@@ -161,6 +162,9 @@ _SIGS = {
     "nk_attention_gqa": (_i32, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32,
                                 _i64, _i32, _f, _p, _i32, _p, _sz, _p]),
     "nk_attention_check": (_i32, [_p, _p, _p]),
+    "nk_embedding_lookup": (_i32, [_p, _i32, _sz, _p, _i64, _i64, _i64, _p, _i32, _sz, _i32, _p]),
+    "nk_add_rms_norm_rows": (_i32, [_p, _p, _i64, _i64, _p, _sz, _f, _p, _p, _i32, _p]),
+    "nk_argmax_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
     "nk_set_stage_timing": (_i32, [_i32]),
     "nk_moe_stage_times": (_i32, [_p, _i32, _p]),
 }
@@ -597,3 +601,60 @@ def attention_check(workspace, stream=None) -> int:
     r = ctypes.c_int64(0)
     call("nk_attention_check", ptr(workspace), ctypes.byref(r), stream_ptr(stream))
     return r.value
+
+
+# ------------------------------------------------- decoder steps around projections
+def _dtype_code(t):
+    import torch
+
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def embedding_lookup(table, token_ids, vocab_size, hidden_size, *, out=None, out_dtype=None,
+                     check=True, stream=None):
+    """embedding_lookup (embedding.rs:73-91); token_ids int32 on the device."""
+    import torch
+
+    _require_cuda(table, token_ids, out)
+    n = token_ids.numel()
+    if out is None:
+        dt = out_dtype or table.dtype
+        out = torch.empty(n, hidden_size, dtype=dt, device=table.device)
+    call("nk_embedding_lookup", ptr(table), _dtype_code(table), table.numel(), ptr(token_ids), n,
+         vocab_size, hidden_size, ptr(out), _dtype_code(out), out.numel(), 1 if check else 0,
+         stream_ptr(stream))
+    return out
+
+
+def add_rms_norm_rows(residual, delta, weight, epsilon, *, h_out=None, normed=None,
+                      normed_dtype=BF16, stream=None):
+    """Block residual (block.rs:145-151) fused with the next RMSNorm; returns (h, normed)."""
+    import torch
+
+    _require_cuda(residual, delta, weight, h_out, normed)
+    rows, width = residual.shape
+    h_out = residual if h_out is None else h_out
+    if normed is None:
+        normed = torch.empty(rows, width, device=residual.device,
+                             dtype=torch.bfloat16 if normed_dtype == BF16 else torch.float32)
+    call("nk_add_rms_norm_rows", ptr(residual), ptr(delta), rows, width, ptr(weight),
+         weight.numel(), epsilon, ptr(h_out), ptr(normed), _dtype_code(normed),
+         stream_ptr(stream))
+    return h_out, normed
+
+
+def argmax_rows(x, *, out=None, stream=None):
+    """predict_next_token's pick (model.rs:325-337) per row of x [rows, n]."""
+    import torch
+
+    _require_cuda(x, out)
+    rows, n = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    call("nk_argmax_rows", ptr(x), _dtype_code(x), rows, n, x.stride(0), ptr(out),
+         stream_ptr(stream))
+    return out

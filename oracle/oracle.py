@@ -381,3 +381,115 @@ def attention(q, k, v, batch, q_seq, kv_seq, q_heads, kv_heads, head_dim, causal
                              ctypes.c_size_t(ol), ctypes.byref(err))
     _check(rc, err)
     return out[:ol]
+
+
+# ------------------------------------------------------------ decoder composition
+
+def _bf16(a):
+    """Round-to-nearest-even to bf16, kept in f32 (the serving path's operand type)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    out = r.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(a), a, out).astype(np.float32)
+
+
+def embedding(table, token_ids, vocab, hidden):
+    """embedding_lookup_into_host (embedding.rs:73-91, validation :121-191)."""
+    table = np.asarray(table, np.float32).reshape(-1)
+    if vocab == 0 or hidden == 0:
+        raise ValueError("InvalidShape")
+    if table.size != vocab * hidden:
+        raise ValueError("LengthMismatch table")
+    ids = np.asarray(token_ids, np.int64).reshape(-1)
+    for t in ids:
+        if t >= vocab or t < 0:
+            raise ValueError(f"TokenOutOfRange {t}")
+    return table.reshape(vocab, hidden)[ids].copy()
+
+
+def argmax_total(row):
+    """predict_next_token's pick (model.rs:325-337): max under f32::total_cmp,
+    the last index among equal maxima (Iterator::max_by)."""
+    u = np.asarray(row, np.float32).view(np.uint32).astype(np.uint64)
+    key = np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    m = key.max()
+    return int(np.nonzero(key == m)[0][-1])
+
+
+def _linear_rows(x, w_out_in):
+    """LinearProjection::project with W given [out, in] (orc.linear takes [in, out])."""
+    rows = x.shape[0]
+    n_out, n_in = w_out_in.shape
+    return linear(np.ascontiguousarray(w_out_in.T), None, n_in, n_out, x.reshape(-1),
+                  rows).reshape(rows, n_out)
+
+
+def mamba2_fused_block(x, w_in, w_out, conv, a_head, d_head, norm_w, heads, head_dim, groups,
+                       state, kernel_size, eps, batch, seq, conv_state=None, ssm_state=None):
+    """The fused-layout Mamba2 block restated on the reference stages: in_proj
+    (rows z | x | B | C | dt), then mamba2_glue on the per-channel expansion
+    (dt, A, D per head; B, C per group), then out_proj of the bf16-rounded
+    normed rows.  Returns (y, new conv_state, new ssm_state)."""
+    C = heads * head_dim
+    T = x.shape[0]
+    fused = _linear_rows(_bf16(x), w_in)
+    z, xs = fused[:, :C], fused[:, C:2 * C]
+    bg = fused[:, 2 * C:2 * C + groups * state].reshape(T, groups, state)
+    cg = fused[:, 2 * C + groups * state:2 * C + 2 * groups * state].reshape(T, groups, state)
+    dth = fused[:, 2 * C + 2 * groups * state:]
+    head, grp = np.arange(C) // head_dim, np.arange(C) // (C // groups)
+    normed, new_conv, fin = mamba2_glue(
+        xs, dth[:, head], bg[:, grp, :].reshape(T, C * state), cg[:, grp, :].reshape(T, C * state),
+        z, conv, np.repeat(a_head[head][:, None], state, axis=1), norm_w, eps, batch, seq, C,
+        state, kernel_size, d=d_head[head], conv_state=conv_state, ssm_state=ssm_state)
+    return _linear_rows(_bf16(normed), w_out), new_conv, fin
+
+
+def decoder_forward(cfg, w, tokens, batch, seq, state=None):
+    """NemotronModel::forward_tokens (model.rs:258-323) over NemotronBlock::forward_into
+    (block.rs:84-157) with the serving path's bf16 operand rounding: the
+    normed block inputs, attention q/k/v/o and the MoE inputs are rounded to
+    bf16 as the device path feeds its GEMMs.  `w` holds host (numpy) weights:
+    embed [V,H], lm_head [V,H], norms [L+1][H], layers[i] dicts.  `state`
+    (optional, updated) carries per-layer caches: attention (k, v) lists,
+    Mamba (conv, ssm).  Returns logits of every row [batch*seq, V]."""
+    H, eps = cfg.hidden, cfg.eps
+    h = embedding(w["embed"], tokens, cfg.vocab, H)
+    if state is None:
+        state = [None] * len(cfg.layer_kinds)
+    for i, kind in enumerate(cfg.layer_kinds):
+        normed = _bf16(rms_norm_rows(h, w["norms"][i], eps, H).reshape(-1, H))
+        lw = w["layers"][i]
+        if kind == "mamba":
+            st = state[i] or (None, None)
+            m, cs, ss = mamba2_fused_block(normed, lw["w_in"], lw["w_out"], lw["conv"], lw["a"],
+                                           lw["d"], lw["norm"], cfg.mamba_heads,
+                                           cfg.mamba_head_dim, cfg.mamba_groups, cfg.mamba_state,
+                                           cfg.conv_kernel, eps, batch, seq, st[0], st[1])
+            state[i] = (cs, ss)
+        elif kind == "moe":
+            Is = cfg.shared_inter
+            m, _, _ = moe(H, cfg.experts, cfg.top_k, cfg.moe_inter, Is, lw["router"].T.copy(),
+                          None, lw["up"].transpose(0, 2, 1).copy(), None,
+                          lw["down"].transpose(0, 2, 1).copy(), None,
+                          lw["sup"].T.copy() if Is else None, None,
+                          lw["sdown"].T.copy() if Is else None, None, normed, normed.shape[0],
+                          cfg.route_mode)
+            m = m.reshape(-1, H)
+        else:
+            hq, hkv, d = cfg.q_heads, cfg.kv_heads, cfg.head_dim
+            q = _bf16(_linear_rows(normed, lw["wq"])).reshape(batch, seq, hq, d)
+            k = _bf16(_linear_rows(normed, lw["wk"])).reshape(batch, seq, hkv, d)
+            v = _bf16(_linear_rows(normed, lw["wv"])).reshape(batch, seq, hkv, d)
+            prev = state[i]
+            if prev is not None:
+                k = np.concatenate([prev[0], k], axis=1)
+                v = np.concatenate([prev[1], v], axis=1)
+            state[i] = (k, v)
+            L = k.shape[1]
+            o = attention(q, k, v, batch, seq, L, hq, hkv, d, causal=True, q_offset=L - seq)
+            m = _linear_rows(_bf16(o.reshape(batch * seq, hq * d)), lw["wo"])
+        h = h + m.reshape(h.shape)
+    normed = _bf16(rms_norm_rows(h, w["norms"][-1], eps, H).reshape(-1, H))
+    return _linear_rows(normed, w["lm_head"]), state
