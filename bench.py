@@ -371,6 +371,60 @@ def mamba_block(torch, dev, world, w_in, w_out, x, reps):
             "scan_unit": "G state updates/s (per GPU)", "n_gpus": world}
 
 
+def decoder_e2e(torch, dev, batch=64, prompt_len=1024, gen=256):
+    """the random-initialised 52-layer hybrid decoder
+    (23 Mamba2, 23 MoE as config 3, 6 GQA attention; hidden 2688, vocab
+    131072) on one GPU: prefill `batch` prompts of `prompt_len` random ids,
+    then greedy-decode `gen` tokens per sequence reusing the KV / conv / SSM
+    states.  Device time with CUDA events; tokens/s counts generated tokens."""
+    import nk
+    import nk_model
+
+    cfg = nk_model.DecoderConfig()
+    model = nk_model.Decoder(cfg, device=dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab, (batch, prompt_len), device=dev, generator=g,
+                           dtype=torch.int32)
+    model.generate(prompt[:, :64], 4)  # warm-up: kernels, workspaces, clocks
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    state = model.new_state(batch, prompt_len + gen)
+    out = torch.empty(batch, gen, dtype=torch.int32, device=dev)
+    ev[0].record()
+    logits = model.forward(prompt.reshape(-1).contiguous(), batch, prompt_len, state)
+    tok = nk.argmax_rows(logits)
+    ev[1].record()
+    for step in range(gen):
+        out[:, step] = tok
+        if step + 1 == gen:
+            break
+        logits = model.forward(tok, batch, 1, state)
+        tok = nk.argmax_rows(logits)
+    ev[2].record()
+    ev[2].synchronize()
+    prefill_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    total = prefill_ms + decode_ms
+    weights_gb = sum(t.numel() * t.element_size() for t in _decoder_tensors(model)) / 1e9
+    return {"config": "52-layer hybrid decoder (pattern " + cfg.pattern + "), hidden 2688, "
+                      "vocab 131072, MoE 128x1856 top-6 + shared 3712, GQA 32/2 x 128, Mamba2 "
+                      "64 heads x 64, 8 groups, d_state 128; batch 64, prompt 1024, greedy 256",
+            "tokens_per_s": round(batch * gen / (total / 1e3), 1),
+            "prefill_ms": round(prefill_ms, 2), "decode_ms": round(decode_ms, 2),
+            "prefill_tokens_per_s": round(batch * prompt_len / (prefill_ms / 1e3)),
+            "decode_ms_per_step": round(decode_ms / max(gen - 1, 1), 3),
+            "weights_gb": round(weights_gb, 2), "n_gpus": 1,
+            "first_tokens": out[0, :8].tolist()}
+
+
+def _decoder_tensors(model):
+    yield model.embed
+    yield model.lm_head
+    for kind, layer in model.layers:
+        for v in layer.raw.values():
+            if v is not None:
+                yield v
+
+
 class EpTimer:
     """Wraps nk_ep.NkBackend and times its stages with CUDA events on the
     current stream (dispatch, grouped experts, shared + combine); the rest of
@@ -655,6 +709,8 @@ def nk_arm(args):
         }
         if args.tp:
             line["tp_projections"] = tp_result
+        if args.e2e and world == 1:
+            line["e2e_decoder"] = decoder_e2e(torch, dev)
         if world == 1 and args.sweep:
             line["gemm_sweep"] = gemm_sweep(torch, nk, dev)
         if world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
@@ -706,6 +762,9 @@ def main():
                     help="also time config 4's tensor-parallel projections")
     ap.add_argument("--sweep", action="store_true",
                     help="also time the config-2 dense / int8 GEMM sweep (adds ~1 min)")
+    ap.add_argument("--e2e", action="store_true",
+                    help="also run config 5: the 52-layer decoder, batch 64, prompt 1024, "
+                         "256 greedy tokens (1 GPU; adds ~1 min)")
     ap.add_argument("--graph", action="store_true",
                     help="replay the forward as a captured CUDA graph (measured no faster "
                          "than eager launches: the step is device-bound)")

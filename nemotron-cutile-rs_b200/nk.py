@@ -386,12 +386,21 @@ class MoeLayer:
         call("nk_moe_workspace_bytes", ctypes.byref(self._struct), tokens, ctypes.byref(b))
         return b.value
 
-    def forward(self, x, out=None, out_dtype=None, indices=None, weights=None, stream=None):
+    def forward(self, x, out=None, out_dtype=None, indices=None, weights=None, stream=None,
+                workspace=None):
+        """workspace: an optional uint8 device buffer shared by several layers
+        (grown in place, as a one-element list [tensor]); by default the layer
+        keeps its own."""
         import torch
 
         t = x.shape[0]
         need = self.workspace_bytes(t)
-        if self._ws is None or self._ws.numel() < need:
+        if workspace is not None:
+            if workspace[0] is None or workspace[0].numel() < need:
+                workspace[0] = None
+                workspace[0] = torch.empty(need, dtype=torch.uint8, device=x.device)
+            self._ws = workspace[0]
+        elif self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
         if out is None:
             out = torch.empty((t, self.weights.hidden), dtype=out_dtype or torch.float32,

@@ -68,13 +68,17 @@ class AttentionMixer:
         self.hq, self.hkv, self.d = q_heads, kv_heads, head_dim
         self.ws = None
 
-    def forward(self, x, batch, seq, cache: nk.KvCache):
+    def forward(self, x, batch, seq, cache: nk.KvCache, workspace=None):
+        """workspace: optional one-element list holding a buffer shared by layers."""
         q = nk.gemm(x, self.wq, out_dtype=torch.bfloat16)
         k = nk.gemm(x, self.wk, out_dtype=torch.bfloat16)
         v = nk.gemm(x, self.wv, out_dtype=torch.bfloat16)
         cache.append(k, v, seq)
-        o, self.ws = nk.attention_gqa(q, cache, seq, self.hq, causal=True, out_dtype=nk.BF16,
-                                      workspace=self.ws)
+        slot = workspace if workspace is not None else [self.ws]
+        o, slot[0] = nk.attention_gqa(q, cache, seq, self.hq, causal=True, out_dtype=nk.BF16,
+                                      workspace=slot[0])
+        if workspace is None:
+            self.ws = slot[0]
         return nk.gemm(o, self.wo, out_dtype=torch.float32)
 
 
@@ -95,6 +99,8 @@ class Decoder:
         self.lm_head = w.get("lm_head", randn(cfg.vocab, H))
         self.norms = w.get("norms", [1.0 + randn(H, std=0.1, dtype=torch.float32)
                                      for _ in range(len(cfg.layer_kinds) + 1)])
+        self.moe_ws = [None]   # one workspace shared by the MoE layers
+        self.attn_ws = [None]  # and one by the attention layers
         self.layers = []
         for i, kind in enumerate(cfg.layer_kinds):
             lw = w.get(("layer", i))
@@ -182,9 +188,9 @@ class Decoder:
             if kind == "mamba":
                 m = layer.forward(normed, batch, seq, conv_state=st[0], ssm_state=st[1])
             elif kind == "moe":
-                m = layer.forward(normed, out_dtype=torch.float32)
+                m = layer.forward(normed, out_dtype=torch.float32, workspace=self.moe_ws)
             else:
-                m = layer.forward(normed, batch, seq, st)
+                m = layer.forward(normed, batch, seq, st, workspace=self.attn_ws)
             h, normed = nk.add_rms_norm_rows(h, m, self.norms[i + 1], c.eps)
         if logits_rows == "last" and seq > 1:
             last = normed.view(batch, seq, c.hidden)[:, -1].contiguous()
