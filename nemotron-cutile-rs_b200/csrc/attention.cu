@@ -113,43 +113,46 @@ __global__ void kv_append_kernel(const __nv_bfloat16 *__restrict__ k_new,
 }
 
 // --------------------------------------------------------------- GQA path
-// q [B, S, Hq, d] -> qp [B, Hkv, S, G, d] (pairs p0 .. p0+np-1 only).
-__global__ void q_regroup_kernel(const uint4 *__restrict__ q, int S, int Hq, int Hkv, int dv,
-                                 int64_t p0, int64_t np, uint4 *__restrict__ qp) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// q [B, S, Hq, d] -> qp [B, Hkv, S, G, d] (pairs p0 .. p0+np-1 only).  A
+// thread moves 16 bytes; 256 / dv rows per block (dv = d/8 chunks per row);
+// the row index is decomposed once per row in 32-bit arithmetic.
+__global__ void __launch_bounds__(256) q_regroup_kernel(const uint4 *__restrict__ q, int S,
+                                                        int Hq, int Hkv, int dv, int p0,
+                                                        int rows, uint4 *__restrict__ qp) {
+  const int rpb = 256 / dv;
+  const int r = blockIdx.x * rpb + (int)threadIdx.x / dv;  // ((lp * S) + s) * G + g
+  const int c = (int)threadIdx.x % dv;
+  if (r >= rows || (int)threadIdx.x >= rpb * dv) return;
   const int G = Hq / Hkv;
-  const int64_t total = np * S * G * dv;
-  if (i >= total) return;
-  const int c = (int)(i % dv);
-  int64_t r = i / dv;  // local row: ((p - p0) * S + s) * G + g
-  const int g = (int)(r % G);
-  r /= G;
-  const int s = (int)(r % S);
-  const int64_t p = p0 + r / S;
-  const int64_t b = p / Hkv, kh = p % Hkv;
-  qp[i] = q[(((b * S + s) * Hq) + kh * G + g) * dv + c];
+  const int g = r % G, sr = r / G, s = sr % S, p = p0 + sr / S;
+  const int b = p / Hkv, kh = p % Hkv;
+  qp[(int64_t)r * dv + c] = q[(((int64_t)b * S + s) * Hq + kh * G + g) * dv + c];
 }
 
-// op [pairs, S, G, d] f32 (local) -> out [B, S, Hq, d] of dtype out_f32 ? f32 : bf16.
-__global__ void o_scatter_kernel(const float *__restrict__ op, int S, int Hq, int Hkv,
-                                 int d, int64_t p0, int64_t np, void *__restrict__ out,
-                                 int out_f32) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// op [pairs, S, G, d] f32 (local) -> out [B, S, Hq, d] (f32 or bf16).  A
+// thread moves 4 values; 256 / (d/4) rows per block.
+__global__ void __launch_bounds__(256) o_scatter_kernel(const float4 *__restrict__ op, int S,
+                                                        int Hq, int Hkv, int d4, int p0,
+                                                        int rows, void *__restrict__ out,
+                                                        int out_f32) {
+  const int rpb = 256 / d4;
+  const int r = blockIdx.x * rpb + (int)threadIdx.x / d4;
+  const int c = (int)threadIdx.x % d4;
+  if (r >= rows || (int)threadIdx.x >= rpb * d4) return;
   const int G = Hq / Hkv;
-  const int64_t total = np * S * G * d;
-  if (i >= total) return;
-  const int dd = (int)(i % d);
-  int64_t r = i / d;
-  const int g = (int)(r % G);
-  r /= G;
-  const int s = (int)(r % S);
-  const int64_t p = p0 + r / S;
-  const int64_t b = p / Hkv, kh = p % Hkv;
-  const int64_t o = (((b * S + s) * Hq) + kh * G + g) * d + dd;
-  if (out_f32)
-    reinterpret_cast<float *>(out)[o] = op[i];
-  else
-    reinterpret_cast<__nv_bfloat16 *>(out)[o] = __float2bfloat16_rn(op[i]);
+  const int g = r % G, sr = r / G, s = sr % S, p = p0 + sr / S;
+  const int b = p / Hkv, kh = p % Hkv;
+  const float4 v = op[(int64_t)r * d4 + c];
+  const int64_t o = (((int64_t)b * S + s) * Hq + kh * G + g) * d4 + c;  // in float4 units
+  if (out_f32) {
+    reinterpret_cast<float4 *>(out)[o] = v;
+  } else {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t *>(&lo);
+    pk.y = *reinterpret_cast<uint32_t *>(&hi);
+    reinterpret_cast<uint2 *>(out)[o] = pk;
+  }
 }
 
 // Score tiles: block = one pair (p0 + blockIdx.x); thread = token tile.  Key
@@ -219,8 +222,69 @@ __global__ void value_tiles_kernel(int np, int S, int G, int d, int bn, int64_t 
 }
 
 // Row softmax of one score row (local row r = (lp * S + s) * G + g): keys
-// 0..lim get exp(scale*S - max) / sum, keys lim+1 .. kpad-1 get 0.  f32 exp,
-// f64 partition as attention.rs:232-251.  A block of 128 threads per row.
+// 0..lim get exp(scale*S - max) / sum, keys lim+1 .. kpad-1 get 0.  f32 exp
+// as attention.rs:232-251; the partition is summed in f32 within a lane
+// (at most VPT terms, each <= 1) and in f64 across lanes.
+__device__ __forceinline__ void flag_row(unsigned long long *bad, int64_t r, int S, int G,
+                                         int64_t p0, int Hq, int Hkv) {
+  const int g = (int)(r % G), s = (int)((r / G) % S);
+  const int64_t p = p0 + r / ((int64_t)S * G);
+  const int64_t b = p / Hkv, kh = p % Hkv;
+  atomicMin(bad, (unsigned long long)(((b * S + s) * Hq) + kh * G + g));
+}
+
+// Warp per row, the row in registers (VPT values per lane, kpad <= 32 * VPT).
+template <int VPT>
+__global__ void __launch_bounds__(256) attn_softmax_warp_kernel(
+    const float *__restrict__ S_, int64_t lds, int S, int G, int L, int kpad, int causal,
+    int64_t q_offset, float scale, int64_t p0, int Hq, int Hkv, __nv_bfloat16 *__restrict__ P,
+    int64_t ldp, int64_t rows, unsigned long long *bad_target) {
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int s = (int)((r / G) % S);
+  int64_t lim = L - 1;
+  if (causal) {
+    const int64_t l = q_offset + s;
+    lim = l < L - 1 ? l : L - 1;
+  }
+  const float *sr = S_ + r * lds;
+  float v[VPT];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int j = lane + 32 * i;
+    v[i] = -INFINITY;
+    if (j <= lim) {
+      const float t = sr[j] * scale;
+      if (isfinite(t)) v[i] = t;
+    }
+    mx = fmaxf(mx, v[i]);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  __nv_bfloat16 *pr = P + r * ldp;
+  if (!isfinite(mx)) {
+    if (lane == 0) flag_row(bad_target, r, S, G, p0, Hq, Hkv);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+      if (lane + 32 * i < kpad) pr[lane + 32 * i] = __float2bfloat16_rn(0.0f);
+    return;
+  }
+  float part_f = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    v[i] = v[i] == -INFINITY ? 0.0f : expf(v[i] - mx);
+    part_f += v[i];
+  }
+  double part = (double)part_f;
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  const float inv = (float)(1.0 / part);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i)
+    if (lane + 32 * i < kpad) pr[lane + 32 * i] = __float2bfloat16_rn(v[i] * inv);
+}
+
+// Rows longer than the register kernels take: a block of 128 threads per row.
 __global__ void __launch_bounds__(128) attn_softmax_kernel(
     const float *__restrict__ S_, int64_t lds, int S, int G, int L, int kpad, int causal,
     int64_t q_offset, float scale, int64_t p0, int Hq, int Hkv, __nv_bfloat16 *__restrict__ P,
@@ -246,20 +310,16 @@ __global__ void __launch_bounds__(128) attn_softmax_kernel(
   __syncthreads();
   mx = fmaxf(fmaxf(red_f[0], red_f[1]), fmaxf(red_f[2], red_f[3]));
   if (!isfinite(mx)) {
-    if (threadIdx.x == 0) {
-      const int g = (int)(r % G);
-      const int64_t p = p0 + r / ((int64_t)S * G);
-      const int64_t b = p / Hkv, kh = p % Hkv;
-      atomicMin(bad_target, (unsigned long long)(((b * S + s) * Hq) + kh * G + g));
-    }
+    if (threadIdx.x == 0) flag_row(bad_target, r, S, G, p0, Hq, Hkv);
     for (int64_t j = threadIdx.x; j < kpad; j += blockDim.x) pr[j] = __float2bfloat16_rn(0.0f);
     return;
   }
-  double part = 0.0;
+  float part_f = 0.0f;
   for (int64_t j = threadIdx.x; j <= lim; j += blockDim.x) {
     const float v = sr[j] * scale;
-    if (isfinite(v)) part += (double)expf(v - mx);
+    if (isfinite(v)) part_f += expf(v - mx);
   }
+  double part = (double)part_f;
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red_d[threadIdx.x >> 5] = part;
@@ -479,9 +539,9 @@ nk_status nk_attention_gqa(const uint16_t *q, const uint16_t *k_cache, const uin
     const int64_t np = pairs - p0 < np_max ? pairs - p0 : np_max;
     const int64_t rows = np * g.S * G;
     const int dv = (int)(g.d / 8);  // uint4 per head row
-    q_regroup_kernel<<<(unsigned)ceil_div(rows * dv, 256), 256, 0, s>>>(
-        reinterpret_cast<const uint4 *>(q), (int)g.S, (int)g.Hq, (int)g.Hkv, dv, p0, np,
-        reinterpret_cast<uint4 *>(w.qp));
+    q_regroup_kernel<<<(unsigned)ceil_div(rows, 256 / dv), 256, 0, s>>>(
+        reinterpret_cast<const uint4 *>(q), (int)g.S, (int)g.Hq, (int)g.Hkv, dv, (int)p0,
+        (int)rows, reinterpret_cast<uint4 *>(w.qp));
     score_tiles_kernel<<<(unsigned)np, 1024, 0, s>>>((int)np, (int)g.S, (int)G, (int)g.L, g.Lmax,
                                                      bn, causal, q_offset, p0, w.score_tiles,
                                                      w.counts);
@@ -503,9 +563,23 @@ nk_status nk_attention_gqa(const uint16_t *q, const uint16_t *k_cache, const uin
                    num_sms(), s);
       if (st != NK_OK) return st;
     }
-    attn_softmax_kernel<<<(unsigned)rows, 128, 0, s>>>(
-        w.s, lds, (int)g.S, (int)G, (int)g.L, (int)kpad, causal, q_offset, sc, p0, (int)g.Hq,
-        (int)g.Hkv, reinterpret_cast<__nv_bfloat16 *>(w.p), kpad, bad);
+    {
+      __nv_bfloat16 *pb = reinterpret_cast<__nv_bfloat16 *>(w.p);
+      const unsigned wg = (unsigned)ceil_div(rows, 8);
+#define NK_SOFTMAX_WARP(V)                                                                  \
+  attn_softmax_warp_kernel<V><<<wg, 256, 0, s>>>(w.s, lds, (int)g.S, (int)G, (int)g.L,      \
+                                                (int)kpad, causal, q_offset, sc, p0,        \
+                                                (int)g.Hq, (int)g.Hkv, pb, kpad, rows, bad)
+      if (kpad <= 128) NK_SOFTMAX_WARP(4);
+      else if (kpad <= 512) NK_SOFTMAX_WARP(16);
+      else if (kpad <= 1024) NK_SOFTMAX_WARP(32);
+      else if (kpad <= 2048) NK_SOFTMAX_WARP(64);
+      else
+        attn_softmax_kernel<<<(unsigned)rows, 128, 0, s>>>(
+            w.s, lds, (int)g.S, (int)G, (int)g.L, (int)kpad, causal, q_offset, sc, p0,
+            (int)g.Hq, (int)g.Hkv, pb, kpad, bad);
+#undef NK_SOFTMAX_WARP
+    }
     st = check_launch("attn_softmax_kernel");
     if (st != NK_OK) return st;
     {  // O = P · V (the transposed V cache is the weight side)
@@ -522,9 +596,9 @@ nk_status nk_attention_gqa(const uint16_t *q, const uint16_t *k_cache, const uin
                    bn, a, num_sms(), s);
       if (st != NK_OK) return st;
     }
-    o_scatter_kernel<<<(unsigned)ceil_div(rows * g.d, 256), 256, 0, s>>>(
-        w.op, (int)g.S, (int)g.Hq, (int)g.Hkv, (int)g.d, p0, np, out,
-        out_dtype == NK_DTYPE_F32);
+    o_scatter_kernel<<<(unsigned)ceil_div(rows, 256 / (g.d / 4)), 256, 0, s>>>(
+        reinterpret_cast<const float4 *>(w.op), (int)g.S, (int)g.Hq, (int)g.Hkv, (int)(g.d / 4),
+        (int)p0, (int)rows, out, out_dtype == NK_DTYPE_F32);
     st = check_launch("o_scatter_kernel");
     if (st != NK_OK) return st;
   }

@@ -90,7 +90,9 @@ def _gqa_case(seed, B, S_prev, S_new, Hq, Hkv, d, max_len):
     (3, 0, 130, 4, 1, 64, None),      # key tiles above the diagonal skipped
     (2, 70, 1, 32, 2, 128, None),     # decode step, q_offset 70
     (4, 5, 3, 16, 2, 128, "3"),       # chunked pairs
-    (1, 0, 300, 32, 2, 128, "1")])    # prefill with 16 queries x 16 heads tiles
+    (1, 0, 300, 32, 2, 128, "1"),     # prefill with 16 queries x 16 heads tiles
+    (1, 650, 50, 8, 2, 128, None),    # rows of 700 keys (register softmax, 32 per lane)
+    (1, 2097, 3, 4, 2, 64, None)])    # rows of 2100 keys (block softmax)
 def test_attention_gqa_matches_oracle(cuda, monkeypatch, B, S_prev, S_new, Hq, Hkv, d, chunk):
     if chunk:
         monkeypatch.setenv("NK_ATTN_CHUNK", chunk)
