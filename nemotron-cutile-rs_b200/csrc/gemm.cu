@@ -132,6 +132,31 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ part, int splits,
     reinterpret_cast<__nv_bfloat16 *>(y)[i] = __float2bfloat16_rn(acc);
 }
 
+// Launches splitk_reduce_kernel as a programmatic dependent of the previous kernel.
+static nk_status launch_splitk_reduce(const float *part, int splits, int64_t mn, int64_t n,
+                                      const float *bias, bool relu2, void *y, bool y_f32,
+                                      cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ceil_div(mn, 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NK_CUDA_TRY(cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, part, splits, mn, n, bias,
+                                 (int)relu2, y, (int)y_f32));
+  return check_launch("splitk_reduce_kernel");
+}
+
+// Decode-size projections on the weight-streaming kernel (gemv.cu).
+int gemv_splits(int64_t m, int64_t n, int64_t k, int64_t *k_per_split);
+void launch_gemv(int wk, const void *x, bool x_f32, int m, const void *w, int64_t n, int64_t k,
+                 int64_t kps, int splits, float w_scale, const float *row_scale,
+                 const float *bias, int relu2, void *y, int y_f32, float *part,
+                 cudaStream_t s);
+
 // K splits for a projection whose token dimension fits one tile (decode
 // shapes, HBM-bound).  Cost model in bytes moved: the weight stream stretched
 // by wave quantisation (units of work over whole waves of SMs), plus the f32
@@ -196,6 +221,33 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
           x, x_dtype == NK_F32, w, w_scale, zp, row_scale, bias, y, y_dtype == NK_F32, relu2, m,
           k, n);
     return check_launch("proj_simt_kernel");
+  }
+
+  // One or two token rows: stream the weights through registers (gemv.cu);
+  // measured faster than the tensor-core kernel there, slower from 4 rows.
+  // NK_GEMV=0 keeps such shapes on the tensor-core kernel (a tuning probe).
+  static const bool gemv_on = [] {
+    const char *e = getenv("NK_GEMV");
+    return !(e && e[0] == '0');
+  }();
+  if (gemv_on && m <= 2 && (wk == WK_BF16 || wk == WK_INT8) && (k % 16) == 0 &&
+      (x_dtype == NK_BF16 || (k % 4) == 0)) {
+    int64_t kps = 0;
+    const int splits = gemv_splits(m, n, k, &kps);
+    float *part = nullptr;
+    if (splits > 1) {
+      void *b = nullptr;
+      nk_status st = scratch((size_t)splits * m * n * 4, &b, stream);
+      if (st != NK_OK) return st;
+      part = reinterpret_cast<float *>(b);
+    }
+    launch_gemv(wk, x, x_dtype == NK_F32, (int)m, w, n, k, kps, splits, w_scale, row_scale,
+                splits > 1 ? nullptr : bias, splits > 1 ? 0 : (int)relu2, y, y_dtype == NK_F32,
+                part, stream);
+    nk_status st = check_launch("gemv_kernel");
+    if (st != NK_OK || splits == 1) return st;
+    return launch_splitk_reduce(part, splits, m * n, n, bias, relu2, y, y_dtype == NK_F32,
+                                stream);
   }
 
   const uint16_t *xb = reinterpret_cast<const uint16_t *>(x);
@@ -282,19 +334,8 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
   nk_status st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream, pair);
   if (st != NK_OK || splits == 1) return st;
   const int64_t mn = m * n;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ceil_div(mn, 256));
-  cfg.blockDim = dim3(256);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  NK_CUDA_TRY(cudaLaunchKernelEx(&cfg, splitk_reduce_kernel,
-                                 reinterpret_cast<const float *>(buf + part_off), splits, mn,
-                                 n, bias, (int)relu2, y, (int)(y_dtype == NK_F32)));
-  return check_launch("splitk_reduce_kernel");
+  return launch_splitk_reduce(reinterpret_cast<const float *>(buf + part_off), splits, mn, n,
+                              bias, relu2, y, y_dtype == NK_F32, stream);
 }
 
 }  // namespace nk

@@ -176,3 +176,30 @@ def test_gemm_cta_pair_path_matches_single_cta(cuda):
     assert r.returncode == 0, r.stderr[-2000:]
     e1, e2 = map(float, r.stdout.split())
     assert e1 <= FP32_TOL and e2 <= FP32_TOL
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+@pytest.mark.parametrize("m,k,n,xf32", [(1, 4096, 21504, False), (4, 4096, 3000, False), (16, 4096, 3000, False),
+                                        (2, 21504, 512, False), (3, 1024, 333, True),
+                                        (12, 2048, 64, True), (9, 8, 5, False)])
+def test_decode_weight_stream_matches_oracle(cuda, kind, m, k, n, xf32):
+    """Projections of <= 16 tokens take the weight-streaming kernel (gemv.cu):
+    bf16 or int8-row weights, bf16 or f32 activations, split K, bias + relu2."""
+    r = rng(m * 7 + k + n)
+    x = r.standard_normal((m, k)).astype(np.float32)
+    if not xf32:
+        x = bf16_round(x)
+    w = (r.standard_normal((n, k)) * 0.02).astype(np.float32)
+    b = r.standard_normal(n).astype(np.float32)
+    if kind == "bf16":
+        wr = bf16_round(w)
+        wd, scales = dev(wr, torch.bfloat16), None
+    else:
+        q, s = nk.quantize_int8_row(dev(w))
+        wr = host(q).astype(np.float32) * host(s)[:, None]
+        wd, scales = q, s
+    ref = _oracle_proj(x, wr, b, relu2=True)
+    xd = dev(x) if xf32 else dev(x, torch.bfloat16)
+    y = nk.gemm(xd, wd, kind=kind, scales=scales, bias=dev(b), relu2=True)
+    torch.cuda.synchronize()
+    assert rel_err(host(y), ref) <= 1e-3
