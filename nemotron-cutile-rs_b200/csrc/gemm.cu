@@ -151,7 +151,7 @@ static nk_status launch_splitk_reduce(const float *part, int splits, int64_t mn,
 }
 
 // Decode-size projections on the weight-streaming kernel (gemv.cu).
-int gemv_splits(int64_t m, int64_t n, int64_t k, int64_t *k_per_split);
+int gemv_splits(int wk, int64_t n, int64_t k, int64_t *k_per_split);
 void launch_gemv(int wk, const void *x, bool x_f32, int m, const void *w, int64_t n, int64_t k,
                  int64_t kps, int splits, float w_scale, const float *row_scale,
                  const float *bias, int relu2, void *y, int y_f32, float *part,
@@ -233,7 +233,7 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
   if (gemv_on && m <= 2 && (wk == WK_BF16 || wk == WK_INT8) && (k % 16) == 0 &&
       (x_dtype == NK_BF16 || (k % 4) == 0)) {
     int64_t kps = 0;
-    const int splits = gemv_splits(m, n, k, &kps);
+    const int splits = gemv_splits(wk, n, k, &kps);
     float *part = nullptr;
     if (splits > 1) {
       void *b = nullptr;

@@ -4,8 +4,8 @@
 // With a handful of tokens every weight element feeds at most 4 FMAs, so
 // the projection is a pure weight stream (HBM-bound) and the tensor cores buy
 // nothing; what matters is keeping enough bytes in flight and touching every
-// weight byte once.  A warp owns R = 4 weight rows; each lane reads 16
-// consecutive K elements of each row per step (32 bytes of bf16, 16 of int8;
+// weight byte once.  A warp owns R weight rows (4 bf16, 8 int8); each lane
+// reads 16 consecutive K elements of each row per step (32 bytes of bf16, 16 of int8;
 // the next step's are loaded before the current step is used), converts them
 // to f32 in registers and multiplies them with the same 16 K elements of
 // every token row (read through L1: X is small and shared by all warps).
@@ -153,7 +153,7 @@ template <typename WT, typename XT, int MT>
 static void launch_gemv_t(const void *x, int m, const void *w, int64_t n, int64_t k, int64_t kps,
                           int splits, float w_scale, const float *row_scale, const float *bias,
                           int relu2, void *y, int y_f32, float *part, cudaStream_t s) {
-  constexpr int R = 4;
+  constexpr int R = sizeof(WT) == 1 ? 8 : 4;  // 128 weight bytes per lane per step
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ceil_div(n, 8 * R), (unsigned)splits);
   cfg.blockDim = dim3(256);
@@ -185,9 +185,8 @@ static void launch_gemv_m(const void *x, int m, const void *w, int64_t n, int64_
 
 // Splits of K: enough blocks for ~4 per SM, each split >= 2048 K elements,
 // a multiple of 512 (one step of the warp's lanes).
-int gemv_splits(int64_t m, int64_t n, int64_t k, int64_t *k_per_split) {
-  (void)m;
-  const int R = 4;
+int gemv_splits(int wk, int64_t n, int64_t k, int64_t *k_per_split) {
+  const int R = wk == WK_INT8 ? 8 : 4;
   const int64_t blocks_n = ceil_div(n, 8 * R);
   int64_t splits = ceil_div((int64_t)num_sms() * 4, blocks_n);
   const int64_t max_splits = k / 2048 > 1 ? k / 2048 : 1;
