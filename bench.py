@@ -468,9 +468,14 @@ class EpTimer:
         return r
 
     def step_times(self):
+        """Milliseconds per stage name on the compute stream (summed over the
+        exchange phases, whose experts are timed one after the other)."""
         self.ev[-1][1].synchronize()
-        return {self.ev[i][0]: self.ev[i - 1][1].elapsed_time(self.ev[i][1])
-                for i in range(1, len(self.ev))}
+        out = {}
+        for i in range(1, len(self.ev)):
+            name = self.ev[i][0]
+            out[name] = out.get(name, 0.0) + self.ev[i - 1][1].elapsed_time(self.ev[i][1])
+        return out
 
 
 # ---------------------------------------------------------------- arms
@@ -576,7 +581,8 @@ def nk_arm(args):
         if args.exchange == "nccl":
             ep = ExpertParallelMoe(ep_timer, E, H, K)
         else:
-            ep = PeerExpertParallelMoe(ep_timer, E, H, K, max_tokens=T)
+            ep = PeerExpertParallelMoe(ep_timer, E, H, K, max_tokens=T,
+                                       phases=int(os.environ.get("NK_EP_PHASES", "1")))
 
         def fwd():
             out.copy_(ep.forward(x)[0])

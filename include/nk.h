@@ -343,6 +343,17 @@ nk_status nk_ipc_free(void *ptr);
 nk_status nk_ep_plan(const int32_t *counts_all, int32_t ranks, int32_t experts, int32_t rank,
                      int32_t *send_base, int32_t *seg_rows, int32_t *seg_start,
                      int32_t *return_offset, int32_t *received_rows, void *stream);
+/* The same plan with the local experts split into `phases` equal groups that
+ * are received and computed one after the other (the exchange of one phase
+ * overlaps the experts of another).  Phase h's rows start at receive row
+ * h * phase_capacity_rows, ordered [source rank][local expert of the phase];
+ * segment index (h * ranks + s) * (El / phases) + (j % (El / phases)) for
+ * source s and local expert j.  seg_start and send_base are absolute rows.
+ * phases = 1 is nk_ep_plan. */
+nk_status nk_ep_plan_phased(const int32_t *counts_all, int32_t ranks, int32_t experts,
+                            int32_t rank, int32_t phases, int64_t phase_capacity_rows,
+                            int32_t *send_base, int32_t *seg_rows, int32_t *seg_start,
+                            int32_t *return_offset, int32_t *received_rows, void *stream);
 
 /* Gathers x[token] for every route slot and stores it into the owning rank's
  * receive buffer (peer_recv: device array of `ranks` peer base pointers,
@@ -360,6 +371,20 @@ nk_status nk_ep_return(const uint16_t *expert_rows, int64_t hidden, int32_t rank
                        int32_t experts_per_rank, const int32_t *seg_rows,
                        const int32_t *seg_start, const int32_t *return_offset,
                        const uint64_t *peer_out, void *stream);
+/* Phase `phase` of nk_ep_dispatch under nk_ep_plan_phased: only the slots
+ * routed to that phase's local experts move. */
+nk_status nk_ep_dispatch_phase(const uint16_t *x, int64_t tokens, int64_t hidden, int32_t top_k,
+                               const int32_t *indices, const int32_t *slot_pos,
+                               const int32_t *offsets, const int32_t *send_base,
+                               int32_t experts_per_rank, int32_t phases, int32_t phase,
+                               const uint64_t *peer_recv, void *stream);
+/* nk_ep_return for segments first_segment .. first_segment+n_segments-1 of a
+ * phased plan (experts_per_phase = El / phases). */
+nk_status nk_ep_return_segments(const uint16_t *expert_rows, int64_t hidden, int32_t ranks,
+                                int32_t experts_per_phase, int32_t first_segment,
+                                int32_t n_segments, const int32_t *seg_rows,
+                                const int32_t *seg_start, const int32_t *return_offset,
+                                const uint64_t *peer_out, void *stream);
 
 /* ---------------------------------------------------------------- tracing */
 

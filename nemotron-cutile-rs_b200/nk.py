@@ -144,6 +144,10 @@ _SIGS = {
     "nk_ep_plan": (_i32, [_p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p]),
     "nk_ep_dispatch": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p, _p, _i32, _p, _p]),
     "nk_ep_return": (_i32, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p]),
+    "nk_ep_plan_phased": (_i32, [_p, _i32, _i32, _i32, _i32, _i64, _p, _p, _p, _p, _p, _p]),
+    "nk_ep_dispatch_phase": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p, _p, _i32, _i32, _i32, _p,
+                                    _p]),
+    "nk_ep_return_segments": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p]),
     "nk_conv1d": (_i32, [_p, _sz, _p, _sz, _i64, _i64, _i64, _p, _sz, _p]),
     "nk_conv1d_ex": (_i32, [_p, _p]),
     "nk_selective_scan": (_i32, [_p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz,

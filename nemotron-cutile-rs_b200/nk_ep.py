@@ -171,14 +171,17 @@ class PeerExpertParallelMoe:
 
     Per forward: dispatch plan (router, routing, plan; no local gather) ->
     all-gather of the per-expert counts (also the barrier that the previous
-    forward's readers are done) -> nk_ep_plan -> nk_ep_dispatch (x rows into
-    the owners' receive buffers) -> barrier -> grouped experts in place ->
-    nk_ep_return (outputs into the source ranks' result buffers) -> barrier
-    -> shared expert + combine.  Barriers are 1-element NCCL all-reduces on
-    the compute stream.  Buffers hold `max_tokens` tokens per rank."""
+    forward's readers are done) -> nk_ep_plan_phased -> for each of `phases`
+    groups of local experts: nk_ep_dispatch_phase (x rows into the owners'
+    receive buffers) -> barrier -> grouped experts in place ->
+    nk_ep_return_segments (outputs into the source ranks' result buffers);
+    the dispatch of phase h+1 and the return of phase h run on a comm stream
+    beside the experts of phases h and h+1 -> barrier -> shared expert +
+    combine.  Barriers are 1-element NCCL all-reduces.  Buffers hold
+    `max_tokens` tokens per rank (per phase region)."""
 
     def __init__(self, backend: NkBackend, experts: int, hidden: int, top_k: int,
-                 max_tokens: int, group=None):
+                 max_tokens: int, group=None, phases: int = 1):
         import ctypes as C
 
         self.be, self.group = backend, group
@@ -188,8 +191,12 @@ class PeerExpertParallelMoe:
             raise ValueError(f"{experts} experts do not split over {self.G} ranks")
         self.E, self.H, self.K, self.T_max = experts, hidden, top_k, max_tokens
         self.El = experts // self.G
+        # The local experts are received and computed in `phases` groups so
+        # that the exchange of one group overlaps the expert GEMMs of another.
+        self.P = phases if phases > 1 and self.El % phases == 0 else 1
+        self.Elh = self.El // self.P
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.cap_rows = self.G * max_tokens * top_k
+        self.cap_rows = self.G * max_tokens * top_k  # rows one phase region can receive
         self._owned, self._opened = [], []
 
         def shared_buffer(nbytes):
@@ -213,10 +220,10 @@ class PeerExpertParallelMoe:
             return ptr.value, torch.tensor(ptrs, dtype=torch.int64, device=dev)
 
         H2 = hidden * 2
-        self.recv_ptr, self.peer_recv = shared_buffer(self.cap_rows * H2)
+        self.recv_ptr, self.peer_recv = shared_buffer(self.P * self.cap_rows * H2)
         self.out_ptr, self.peer_out = shared_buffer(max_tokens * top_k * H2)
         # local views of the two buffers
-        self.recv = _tensor_at(self.recv_ptr, (self.cap_rows, hidden), dev)
+        self.recv = _tensor_at(self.recv_ptr, (self.P * self.cap_rows, hidden), dev)
         self.out_rows = _tensor_at(self.out_ptr, (max_tokens * top_k, hidden), dev)
         i32 = dict(dtype=torch.int32, device=dev)
         self.send_base = torch.empty(experts, **i32)
@@ -224,10 +231,13 @@ class PeerExpertParallelMoe:
         self.seg_start = torch.empty(self.G * self.El, **i32)
         self.ret_off = torch.empty(self.G * self.El, **i32)
         self.total = torch.empty(1, **i32)
-        self.seg_expert = torch.arange(self.El, **i32).repeat(self.G)
+        # segment order [phase][source][local expert of the phase]
+        self.seg_expert = torch.cat([torch.arange(h * self.Elh, (h + 1) * self.Elh, **i32)
+                                     .repeat(self.G) for h in range(self.P)])
         self.counts_all = torch.empty(self.G * experts, **i32)
         self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
         self.side = torch.cuda.Stream(device=dev)
+        self.comm = torch.cuda.Stream(device=dev)
         dist.barrier(group=group)
 
     def _barrier(self):
@@ -246,16 +256,60 @@ class PeerExpertParallelMoe:
             sh = self.be.shared(x)
         idx, w, counts, offsets, slot_pos = self.be.dispatch(x, gather=False)
         dist.all_gather_into_tensor(self.counts_all, counts, group=self.group)
-        nk.call("nk_ep_plan", nk.ptr(self.counts_all), self.G, self.E, self.me,
-                nk.ptr(self.send_base), nk.ptr(self.seg_rows), nk.ptr(self.seg_start),
-                nk.ptr(self.ret_off), nk.ptr(self.total), s)
-        nk.call("nk_ep_dispatch", nk.ptr(x), t, self.H, self.K, nk.ptr(idx), nk.ptr(slot_pos),
-                nk.ptr(offsets), nk.ptr(self.send_base), self.El, nk.ptr(self.peer_recv), s)
+        nk.call("nk_ep_plan_phased", nk.ptr(self.counts_all), self.G, self.E, self.me, self.P,
+                self.cap_rows, nk.ptr(self.send_base), nk.ptr(self.seg_rows),
+                nk.ptr(self.seg_start), nk.ptr(self.ret_off), nk.ptr(self.total), s)
+        nseg = self.G * self.Elh  # segments per phase
+
+        def dispatch(h, stream):
+            nk.call("nk_ep_dispatch_phase", nk.ptr(x), t, self.H, self.K, nk.ptr(idx),
+                    nk.ptr(slot_pos), nk.ptr(offsets), nk.ptr(self.send_base), self.El, self.P,
+                    h, nk.ptr(self.peer_recv), nk.stream_ptr(stream))
+
+        def experts(h):
+            region = self.recv[h * self.cap_rows:(h + 1) * self.cap_rows]
+            self.be.experts_into(region, self.seg_expert[h * nseg:(h + 1) * nseg],
+                                 self.seg_rows[h * nseg:(h + 1) * nseg], region)
+
+        def give_back(h, stream):
+            nk.call("nk_ep_return_segments", nk.ptr(self.recv), self.H, self.G, self.Elh,
+                    h * nseg, nseg, nk.ptr(self.seg_rows), nk.ptr(self.seg_start),
+                    nk.ptr(self.ret_off), nk.ptr(self.peer_out), nk.stream_ptr(stream))
+
+        # Phase 0 moves on the compute stream; every later phase's rows move on
+        # the comm stream while the previous phase's experts run, and each
+        # phase's results go back on the comm stream while the next phase's
+        # experts run.  Barriers (1-element all-reduces) order the peers.
+        dispatch(0, main)
         self._barrier()
-        self.be.experts_into(self.recv, self.seg_expert, self.seg_rows, self.recv)
-        nk.call("nk_ep_return", nk.ptr(self.recv), self.H, self.G, self.El,
-                nk.ptr(self.seg_rows), nk.ptr(self.seg_start), nk.ptr(self.ret_off),
-                nk.ptr(self.peer_out), s)
+        planned = torch.cuda.Event()
+        planned.record(main)
+        arrived = []
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(planned)
+            for h in range(1, self.P):
+                dispatch(h, self.comm)
+                self._barrier()
+                ev = torch.cuda.Event()
+                ev.record(self.comm)
+                arrived.append(ev)
+        returned = []
+        for h in range(self.P):
+            if h > 0:
+                main.wait_event(arrived[h - 1])
+            experts(h)
+            if h + 1 < self.P:
+                done = torch.cuda.Event()
+                done.record(main)
+                self.comm.wait_event(done)
+                give_back(h, self.comm)
+                ev = torch.cuda.Event()
+                ev.record(self.comm)
+                returned.append(ev)
+            else:
+                give_back(h, main)
+        for ev in returned:
+            main.wait_event(ev)
         self._barrier()
         main.wait_stream(self.side)
         if sh is not None:

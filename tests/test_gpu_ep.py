@@ -44,7 +44,7 @@ def _worker(rank, world, port, q, peer):
                           up_w=local_expert_slice(full.up_w, rank, world, E),
                           down_w=local_expert_slice(full.down_w, rank, world, E))
     be = NkBackend(full, local)
-    ep = (PeerExpertParallelMoe(be, E, H, K, max_tokens=T + 37 * world) if peer
+    ep = (PeerExpertParallelMoe(be, E, H, K, max_tokens=T + 37 * world, phases=peer) if peer
           else ExpertParallelMoe(be, E, H, K))
     xg = torch.Generator(device=dev).manual_seed(10 + rank)
     x = torch.randn(T + 37 * rank, H, device=dev, generator=xg).bfloat16()
@@ -62,7 +62,8 @@ def _worker(rank, world, port, q, peer):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("peer", [False, True], ids=["nccl_all_to_all", "nvlink_peer_stores"])
+@pytest.mark.parametrize("peer", [0, 1, 2], ids=["nccl_all_to_all", "nvlink_peer_stores",
+                                               "nvlink_peer_stores_2_phases"])
 def test_expert_parallel_two_gpus_matches_single_gpu(peer):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
