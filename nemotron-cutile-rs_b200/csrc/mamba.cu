@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(128) scan_kernel(ScanDev p) {
 //     mix = (dt*B)*x, h = exp(dt*A)*h + mix, and the state sum runs in f32;
 //     the transposing lane reduction of scan_kernel then stores 8 steps at once.
 namespace staged {
-constexpr int S = 128, LPC = 8, SPL = 16, U = 8, STAGES = 3;
+constexpr int S = 128, U = 8, STAGES = 3;
 template <int CH>
 struct __align__(16) Stage {
   float b[U][S];
@@ -369,9 +369,13 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int NCH, int THREADS>
+template <int NCH, int THREADS, int LPC>
 __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(ScanDev p) {
   using namespace staged;
+  static_assert(LPC == 8 || LPC == 16, "8 or 16 lanes per channel");
+  constexpr int SPL = S / LPC;           // states per lane
+  constexpr int M4 = SPL / 4;            // float4 groups per lane
+  constexpr int STRIDE = 4 * LPC;        // states between a lane's groups
   constexpr int GROUPS = THREADS / LPC;  // channel slots per block
   constexpr int CH = GROUPS * NCH;       // channels per block
   static_assert(U * (CH / 4) <= THREADS && U <= THREADS, "copy split");
@@ -421,11 +425,11 @@ __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(Sca
 #pragma unroll
   for (int n = 0; n < NCH; ++n)
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
+    for (int m = 0; m < M4; ++m) {
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (p.init)
         v = *reinterpret_cast<const float4 *>(
-            p.init + (bi * p.C + ch0 + cl + GROUPS * n) * S + 32 * m + 4 * sub);
+            p.init + (bi * p.C + ch0 + cl + GROUPS * n) * S + STRIDE * m + 4 * sub);
       h[n][4 * m] = v.x; h[n][4 * m + 1] = v.y; h[n][4 * m + 2] = v.z; h[n][4 * m + 3] = v.w;
     }
 
@@ -469,9 +473,9 @@ __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(Sca
 #pragma unroll
         for (int n = 0; n < NCH; ++n) q[n][0] = q[n][1] = q[n][2] = q[n][3] = 0.0f;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const float4 bv = *reinterpret_cast<const float4 *>(&g.b[u][32 * m + 4 * sub]);
-          const float4 cv = *reinterpret_cast<const float4 *>(&g.c[u][32 * m + 4 * sub]);
+        for (int m = 0; m < M4; ++m) {
+          const float4 bv = *reinterpret_cast<const float4 *>(&g.b[u][STRIDE * m + 4 * sub]);
+          const float4 cv = *reinterpret_cast<const float4 *>(&g.c[u][STRIDE * m + 4 * sub]);
           const float db[4] = {dtv * bv.x, dtv * bv.y, dtv * bv.z, dtv * bv.w};
           const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
@@ -491,6 +495,13 @@ __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(Sca
         }
       }
     }
+    // Butterflies over lane bits >= U, then the transposing halving.
+#pragma unroll
+    for (int o = LPC / 2; o >= U; o >>= 1)
+#pragma unroll
+      for (int n = 0; n < NCH; ++n)
+#pragma unroll
+        for (int u = 0; u < U; ++u) part[n][u] += __shfl_xor_sync(0xffffffffu, part[n][u], o);
 #pragma unroll
     for (int o = U / 2; o >= 1; o >>= 1) {
       const bool up = (sub & o) != 0;
@@ -503,7 +514,7 @@ __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(Sca
           part[n][i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
     }
-    if (sub < nsteps) {
+    if (sub < U && sub < nsteps) {
 #pragma unroll
       for (int n = 0; n < NCH; ++n)
         p.y[(row0 + t0 + sub) * p.ld_y + ch0 + cl + GROUPS * n] = part[n][0];
@@ -515,8 +526,8 @@ __global__ void __launch_bounds__(THREADS, 256 / THREADS) scan_staged_kernel(Sca
 #pragma unroll
     for (int n = 0; n < NCH; ++n)
 #pragma unroll
-      for (int m = 0; m < 4; ++m)
-        *reinterpret_cast<float4 *>(p.fin + (bi * p.C + ch0 + cl + GROUPS * n) * S + 32 * m +
+      for (int m = 0; m < M4; ++m)
+        *reinterpret_cast<float4 *>(p.fin + (bi * p.C + ch0 + cl + GROUPS * n) * S + STRIDE * m +
                                     4 * sub) =
             make_float4(h[n][4 * m], h[n][4 * m + 1], h[n][4 * m + 2], h[n][4 * m + 3]);
   }
@@ -640,7 +651,8 @@ static nk_status launch_scan(const nk_scan_args &a, cudaStream_t s) {
   // 16 states per lane up to S = 128 (8 lanes), then 16 or 32 lanes.
   // Probes (tuning and tests): NK_SCAN_CFG=8 selects 8 states x 16 lanes at
   // S <= 128, =1 the generic kernel where the staged one applies, =2 the
-  // staged kernel with one channel per thread, =3 with 128-thread blocks.
+  // staged kernel with one channel per thread, =3 with 128-thread blocks,
+  // =4 / =5 with 16 lanes per channel (128 / 64 threads).
   int spl = 16, lpc;
   if (a.states <= 16) lpc = 1;
   else if (a.states <= 32) lpc = 2;
@@ -677,32 +689,39 @@ static nk_status launch_scan(const nk_scan_args &a, cudaStream_t s) {
   }
   const dim3 grid((unsigned)ceil_div(a.channels * lpc, 128), (unsigned)a.batch);
   const bool aps = a.a_per_state != 0;
-  // Staged kernel: NCH channels per thread, 8 lanes per channel slot, all of
-  // a block's channels in one dt/A head and one B/C group.  Default: 2
-  // channels per thread in 64-thread blocks (16 channels per block).
-  int nch = 2, threads = 64;
+  // Staged kernel: NCH channels per thread, LPC lanes per channel slot, all
+  // of a block's channels in one dt/A head and one B/C group.  Default: 2
+  // channels per thread, 8 lanes, 64-thread blocks (16 channels per block).
+  int nch = 2, threads = 64, slpc = 8;
   if (env && atoi(env) == 2) nch = 1;
   if (env && atoi(env) == 3) threads = 128;
-  auto staged_fits = [&](int nc, int th) {
-    const int64_t ch = (int64_t)(th / staged::LPC) * nc;
+  if (env && atoi(env) == 4) { slpc = 16; threads = 128; }
+  if (env && atoi(env) == 5) slpc = 16;
+  auto staged_fits = [&](int nc, int th, int lp) {
+    const int64_t ch = (int64_t)(th / lp) * nc;
     return !aps && a.states == staged::S && a.channels % ch == 0 && a.dt_group % ch == 0 &&
            a.a_group % ch == 0 && a.bc_group % ch == 0 && a.ld_bc % 4 == 0 &&
            a.ld_x % 4 == 0 && aligned16(a.b) && aligned16(a.c) && aligned16(a.x) &&
            (!a.initial_state || aligned16(a.initial_state)) &&
            (!a.final_state || aligned16(a.final_state)) && !(env && atoi(env) == 1);
   };
-  if (!staged_fits(nch, threads)) {
+  if (!staged_fits(nch, threads, slpc)) {
     nch = 1;
     threads = 64;
+    slpc = 8;
   }
-  if (staged_fits(nch, threads)) {
-    const dim3 g((unsigned)(a.channels / ((threads / staged::LPC) * nch)), (unsigned)a.batch);
-    if (nch == 2 && threads == 128)
-      scan_staged_kernel<2, 128><<<g, 128, 0, s>>>(p);
+  if (staged_fits(nch, threads, slpc)) {
+    const dim3 g((unsigned)(a.channels / ((threads / slpc) * nch)), (unsigned)a.batch);
+    if (slpc == 16 && threads == 128)
+      scan_staged_kernel<2, 128, 16><<<g, 128, 0, s>>>(p);
+    else if (slpc == 16)
+      scan_staged_kernel<2, 64, 16><<<g, 64, 0, s>>>(p);
+    else if (nch == 2 && threads == 128)
+      scan_staged_kernel<2, 128, 8><<<g, 128, 0, s>>>(p);
     else if (nch == 2)
-      scan_staged_kernel<2, 64><<<g, 64, 0, s>>>(p);
+      scan_staged_kernel<2, 64, 8><<<g, 64, 0, s>>>(p);
     else
-      scan_staged_kernel<1, 64><<<g, 64, 0, s>>>(p);
+      scan_staged_kernel<1, 64, 8><<<g, 64, 0, s>>>(p);
   }
   else if (spl == 8) scan_dispatch<8, 16, 8>(p, vec, aps, grid, s);
   else if (lpc == 1) scan_dispatch<16, 1, 1>(p, vec, aps, grid, s);

@@ -194,6 +194,8 @@ def _expand_grouped(T, C, S, H, G, r, a_h, d_h):
                                              (2, 37, 128, 128, 4, 2, None),
                                              (2, 37, 128, 128, 4, 2, "1"),
                                              (2, 37, 128, 128, 4, 2, "2"),
+                                             (2, 37, 128, 128, 4, 2, "4"),
+                                             (3, 16, 256, 128, 4, 2, "5"),
                                              (1, 19, 96, 128, 6, 2, "2"),
                                              (1, 5, 64, 128, 2, 1, None),
                                              (3, 16, 256, 128, 4, 2, None)])
