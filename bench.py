@@ -629,21 +629,48 @@ def nk_arm(args):
 
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
-    # e2e: host (pinned) input -> device -> forward -> host output, every step
-    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    for i in range(args.steps):
-        flush()
-        e_starts[i].record(stream)
-        xin.copy_(x_host, non_blocking=True)
-        fwd_e2e()
-        out_host.copy_(out, non_blocking=True)
-        e_ends[i].record(stream)
-    barrier()
+    # e2e: host (pinned) input -> device -> forward -> host output, every step.
+    # One GPU: through the host-buffer executor (nk_moe_pipeline_*), whose
+    # copies of adjacent steps overlap the forward in between.  No separate
+    # L2 flush there: every step streams the experts' weights (1.3-2.6 GB, > the
+    # 126 MB L2) and copies its input in fresh from the host.
+    # Several GPUs: copy in, forward, copy out back to back on one stream.
+    if world == 1:
+        nk.set_stage_timing(False)
+        pstreams = [torch.cuda.Stream(dev) for _ in range(3)]
+        pipe = nk.MoePipeline(layer, T, streams=pstreams)
+        out_hosts = [out_host, torch.empty(T, H, dtype=torch.float32).pin_memory()]
+        for i in range(max(args.warmup, 2)):
+            pipe.submit(x_host, out_hosts[i % 2])
+        pipe.wait()
+        barrier()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record(pstreams[0])
+        pstreams[1].wait_event(e_start)
+        pstreams[2].wait_event(e_start)
+        for i in range(args.steps):
+            pipe.submit(x_host, out_hosts[i % 2])
+        e_end.record(pstreams[2])
+        pipe.wait()
+        barrier()
+        e2e_ms = [e_start.elapsed_time(e_end)]
+        pipe.close()
+    else:
+        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        for i in range(args.steps):
+            flush()
+            e_starts[i].record(stream)
+            xin.copy_(x_host, non_blocking=True)
+            fwd_e2e()
+            out_host.copy_(out, non_blocking=True)
+            e_ends[i].record(stream)
+        barrier()
+        e2e_ms = [s.elapsed_time(e) for s, e in zip(e_starts, e_ends)]
     clocks = sampler.stop()
     nk.device_status()
-    e2e_ms = [s.elapsed_time(e) for s, e in zip(e_starts, e_ends)]
 
     total_ms = sum(step_ms)
     total_e2e = sum(e2e_ms)
@@ -713,6 +740,11 @@ def nk_arm(args):
             "clocks": clocks,
             "gpu_launches": 14 * args.steps * 2,
         }
+        line["config"]["e2e"] = (
+            "nk_moe_pipeline_submit per step (host-buffer executor: pinned x in, f32 out back; "
+            "copies of adjacent steps overlap the forward; no L2 flush: each step streams "
+            "all routed experts' weights, 1.3-2.6 GB > L2)"
+            if world == 1 else "copy in, forward, copy out back to back per step")
         if args.tp:
             line["tp_projections"] = tp_result
         if args.e2e and world == 1:

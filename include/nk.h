@@ -273,6 +273,30 @@ nk_status nk_moe_forward(const nk_moe_layer *layer, const uint16_t *x, int64_t t
                          void *out, int32_t out_dtype, int32_t *indices, float *weights,
                          void *workspace, size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------------ host-buffer MoE executor
+ * MoeLayer::forward_into (moe.rs:154-249) for callers whose activations live
+ * in HOST memory (the reference's *_into_host convention): each submission
+ * copies x_host (bf16 [tokens, H]) to the device, runs nk_moe_forward and
+ * copies out (out_dtype [tokens, H]) and, when indices_host is not NULL, the
+ * routing indices (int32 [tokens, top_k]) back.  Two device slots and three
+ * streams (host->device, compute, device->host) let the copies of adjacent
+ * submissions overlap the forward in between; forwards run in submission
+ * order.  Host buffers must stay valid, and out_host / indices_host unread,
+ * until nk_moe_pipeline_wait returns; page-locked host memory (cudaHostAlloc
+ * / cudaHostRegister) is needed for the copies to overlap.  Streams: all
+ * three given (cudaStream_t) or all NULL (the executor creates its own).
+ * `layer`'s device weights must outlive the executor. */
+typedef struct nk_moe_pipeline nk_moe_pipeline;
+nk_status nk_moe_pipeline_create(const nk_moe_layer *layer, int64_t max_tokens,
+                                 int32_t out_dtype, void *h2d_stream, void *compute_stream,
+                                 void *d2h_stream, nk_moe_pipeline **out);
+nk_status nk_moe_pipeline_submit(nk_moe_pipeline *p, const uint16_t *x_host, int64_t tokens,
+                                 void *out_host, int32_t *indices_host);
+/* Blocks until every submission has completed; then reports a device-side
+ * error like nk_device_status. */
+nk_status nk_moe_pipeline_wait(nk_moe_pipeline *p);
+nk_status nk_moe_pipeline_destroy(nk_moe_pipeline *p);
+
 /* ------------------------------------------ MoE stages (expert parallelism)
  * nk_moe_forward in three separable stages, so that the routed rows can be
  * exchanged between ranks that own disjoint, contiguous ranges of experts

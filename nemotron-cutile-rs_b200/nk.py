@@ -131,6 +131,10 @@ _SIGS = {
     "nk_linear_pack_kn": (_i32, [_p, _i64, _i64, _p, _p]),
     "nk_moe_workspace_bytes": (_i32, [_p, _i64, _p]),
     "nk_moe_forward": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+    "nk_moe_pipeline_create": (_i32, [_p, _i64, _i32, _p, _p, _p, _p]),
+    "nk_moe_pipeline_submit": (_i32, [_p, _p, _i64, _p, _p]),
+    "nk_moe_pipeline_wait": (_i32, [_p]),
+    "nk_moe_pipeline_destroy": (_i32, [_p]),
     "nk_moe_dispatch_workspace_bytes": (_i32, [_p, _i64, _p]),
     "nk_moe_dispatch": (_i32, [_p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "nk_moe_experts_workspace_bytes": (_i32, [_p, _i64, _i32, _p]),
@@ -413,6 +417,52 @@ class MoeLayer:
         call("nk_moe_forward", ctypes.byref(self._struct), ptr(x), t, ptr(out), od, ptr(indices),
              ptr(weights), ptr(self._ws), self._ws.numel(), stream_ptr(stream))
         return out
+
+
+class MoePipeline:
+    """Host-buffer MoE forwards (nk_moe_pipeline_*): submit(x_host, out_host)
+    copies x in, runs the layer and copies out, overlapping the copies of
+    adjacent submissions with the forward in between.  x_host / out_host are
+    CPU tensors (pinned for the copies to overlap); results are valid after
+    wait().  streams: optional (h2d, compute, d2h) torch.cuda.Stream triple."""
+
+    def __init__(self, layer: MoeLayer, max_tokens: int, out_dtype=None, streams=None):
+        import torch
+
+        self.layer = layer  # keeps the weights (and the layer struct) alive
+        self.streams = streams
+        od = BF16 if out_dtype == torch.bfloat16 else F32
+        self.out_dtype = torch.bfloat16 if od == BF16 else torch.float32
+        self.max_tokens = max_tokens
+        h = ctypes.c_void_p()
+        sp = [None, None, None] if streams is None else [s.cuda_stream for s in streams]
+        call("nk_moe_pipeline_create", ctypes.byref(layer._struct), max_tokens, od, *sp,
+             ctypes.byref(h))
+        self._h = h
+
+    def submit(self, x_host, out_host, indices_host=None):
+        for t in (x_host, out_host, indices_host):
+            if t is not None and (t.is_cuda or not t.is_contiguous()):
+                raise ValueError("host tensors must be contiguous CPU tensors")
+        tokens = x_host.shape[0]
+        if out_host.dtype != self.out_dtype or out_host.numel() < tokens * self.layer.weights.hidden:
+            raise ValueError("out_host must hold tokens x hidden values of the pipeline's dtype")
+        call("nk_moe_pipeline_submit", self._h, x_host.data_ptr(), tokens, out_host.data_ptr(),
+             None if indices_host is None else indices_host.data_ptr())
+
+    def wait(self):
+        call("nk_moe_pipeline_wait", self._h)
+
+    def close(self):
+        if self._h:
+            call("nk_moe_pipeline_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def device_status(stream=None) -> None:

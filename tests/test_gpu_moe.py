@@ -97,3 +97,38 @@ def test_moe_bf16_output_and_repeat_determinism(cuda):
     assert torch.equal(a, b)  # deterministic: no atomics in the data path
     c = layer.forward(x, out_dtype=torch.bfloat16)
     assert rel_err(host(c), host(a)) <= BF16_TOL
+
+
+def test_host_pipeline_matches_device_forward(cuda):
+    # nk_moe_pipeline_*: host buffers in and out, copies overlapped across
+    # submissions; every submission's output equals nk_moe_forward's bit for bit.
+    import torch
+
+    T, H, E, K, I = 300, 256, 16, 4, 128
+    g = torch.Generator(device="cuda").manual_seed(11)
+    w = nk.MoeWeights(hidden=H, experts=E, top_k=K, inter=I, shared_inter=192,
+                      route_mode=nk.ROUTE_SIGMOID_RENORM, weight_kind=nk.W_BF16,
+                      router_w3=nk.router_split(torch.randn(E, H, device="cuda", generator=g)),
+                      up_w=(torch.randn(E, I, H, device="cuda", generator=g) * 0.05).bfloat16(),
+                      down_w=(torch.randn(E, H, I, device="cuda", generator=g) * 0.05).bfloat16(),
+                      shared_up_w=(torch.randn(192, H, device="cuda", generator=g) * 0.05).bfloat16(),
+                      shared_down_w=(torch.randn(H, 192, device="cuda", generator=g) * 0.05).bfloat16())
+    layer = nk.MoeLayer(w)
+    pipe = nk.MoePipeline(layer, T)
+    sizes = [T, 1, 77, T, 129]
+    xs = [torch.randn(t, H, generator=torch.Generator().manual_seed(i)).bfloat16().pin_memory()
+          for i, t in enumerate(sizes)]
+    outs = [torch.full((t, H), float("nan")).pin_memory() for t in sizes]
+    idxs = [torch.empty(t, K, dtype=torch.int32).pin_memory() for t in sizes]
+    for x, o, ix in zip(xs, outs, idxs):
+        pipe.submit(x, o, ix)
+    pipe.wait()
+    for x, o, ix in zip(xs, outs, idxs):
+        idx = torch.empty(x.shape[0] * K, dtype=torch.int32, device="cuda")
+        want = layer.forward(x.cuda(), indices=idx)
+        torch.cuda.synchronize()
+        assert torch.equal(o, want.cpu())
+        assert torch.equal(ix.reshape(-1), idx.cpu())
+    with pytest.raises(nk.NkError):
+        pipe.submit(torch.zeros(T + 1, H, dtype=torch.bfloat16), torch.zeros(T + 1, H))
+    pipe.close()
