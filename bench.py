@@ -562,7 +562,6 @@ def nk_arm(args):
     if world == 1:
         layer = nk.MoeLayer(w)
         fwd = lambda: layer.forward(x, out=out, indices=idx)  # noqa: E731
-        fwd_e2e = lambda: layer.forward(xin, out=out, indices=idx)  # noqa: E731
     else:
         from nk_ep import (ExpertParallelMoe, NkBackend, PeerExpertParallelMoe,
                            local_expert_slice)
@@ -587,9 +586,6 @@ def nk_arm(args):
         def fwd():
             out.copy_(ep.forward(x)[0])
 
-        def fwd_e2e():
-            out.copy_(ep.forward(xin)[0])
-
     def barrier():
         if world > 1:
             torch.distributed.barrier()
@@ -604,13 +600,10 @@ def nk_arm(args):
     # With --graph the step replays a CUDA graph captured from the C-ABI call
     # (the 14 kernel launches of one forward), stage-timing events included.
     if args.graph and world == 1:
-        graphs = []
-        for fn in (fwd, fwd_e2e):
-            g_ = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_):
-                fn()
-            graphs.append(g_)
-        fwd, fwd_e2e = graphs[0].replay, graphs[1].replay
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fwd()
+        fwd = graph.replay
     sampler = ClockSampler(local)
     time.sleep(0.2)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -634,7 +627,9 @@ def nk_arm(args):
     # copies of adjacent steps overlap the forward in between.  No separate
     # L2 flush there: every step streams the experts' weights (1.3-2.6 GB, > the
     # 126 MB L2) and copies its input in fresh from the host.
-    # Several GPUs: copy in, forward, copy out back to back on one stream.
+    # Several GPUs: copy in, expert-parallel forward, copy out back to back on
+    # one stream (the same three-stream schedule around the Python-orchestrated
+    # exchange measured slower: 1.6 M against 3.5 M tokens/s at N = 2).
     if world == 1:
         nk.set_stage_timing(False)
         pstreams = [torch.cuda.Stream(dev) for _ in range(3)]
@@ -664,7 +659,7 @@ def nk_arm(args):
             flush()
             e_starts[i].record(stream)
             xin.copy_(x_host, non_blocking=True)
-            fwd_e2e()
+            out.copy_(ep.forward(xin)[0])
             out_host.copy_(out, non_blocking=True)
             e_ends[i].record(stream)
         barrier()
