@@ -14,45 +14,64 @@ namespace nk {
 constexpr int kMoeBN = 256;
 constexpr int kRouterMaxSplits = 16;
 
-// Grouped tile list over row segments: segment s holds seg_rows[s] contiguous
-// rows (segments back to back) for expert seg_expert[s] (identity when null).
-// Each segment gets ceil(n_out/128) feature tiles x ceil(rows/BN) token tiles.
-// One block of 1024 threads; n_seg <= 1024.
-__global__ void build_tiles_kernel(const int32_t *__restrict__ seg_rows,
-                                   const int32_t *__restrict__ seg_expert, int n_seg, int n_out,
-                                   int bn, TcTile *__restrict__ tiles, int *__restrict__ count) {
+// Grouped tile lists over row segments: segment s holds seg_rows[s]
+// contiguous rows (segments back to back) for expert seg_expert[s] (identity
+// when null).  Each segment gets ceil(n_out/128) feature tiles x
+// ceil(rows/BN) token tiles, feature-major within the segment.  Block b
+// builds list b (n_out[b], tiles[b], count[b]): the up and the down
+// projection in one launch.  n_seg <= 1024; after a scan of the per-segment
+// tile counts every thread writes tiles, locating its segment by binary search.
+struct TileLists {
+  int n_out[2];
+  TcTile *tiles[2];
+  int *count[2];
+};
+
+__global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__restrict__ seg_rows,
+                                                           const int32_t *__restrict__ seg_expert,
+                                                           int n_seg, int bn, TileLists lists) {
   __shared__ int tiles_sc[1024];
   __shared__ int rows_sc[1024];
   const int s = threadIdx.x;
+  const int n_out = lists.n_out[blockIdx.x];
+  TcTile *tiles = lists.tiles[blockIdx.x];
   const int ft = (n_out + 127) / 128;
   const int c = s < n_seg ? seg_rows[s] : 0;
-  const int tt = (c + bn - 1) / bn;
-  const int mine = ft * tt;
+  const int mine = ft * ((c + bn - 1) / bn);
   tiles_sc[s] = mine;
   rows_sc[s] = c;
   __syncthreads();
-  for (int o = 1; o < blockDim.x; o <<= 1) {  // inclusive scans of tiles and rows
-    int v = s >= o ? tiles_sc[s - o] : 0;
-    int r = s >= o ? rows_sc[s - o] : 0;
+  for (int o = 1; o < 1024; o <<= 1) {  // inclusive scans of tiles and rows
+    const int v = s >= o ? tiles_sc[s - o] : 0;
+    const int r = s >= o ? rows_sc[s - o] : 0;
     __syncthreads();
     tiles_sc[s] += v;
     rows_sc[s] += r;
     __syncthreads();
   }
-  const int base = tiles_sc[s] - mine, off = rows_sc[s] - c;
-  if (s == blockDim.x - 1) *count = tiles_sc[s];
-  if (s >= n_seg) return;
-  const int e = seg_expert ? seg_expert[s] : s;
-  for (int f = 0; f < ft; ++f)
-    for (int t = 0; t < tt; ++t) {
-      TcTile tile;
-      tile.w_row = e * n_out + f * 128;
-      tile.x_row = off + t * bn;
-      int fv = n_out - f * 128, tv = c - t * bn;
-      tile.valid = ((fv > 128 ? 128 : fv) << 16) | (tv > bn ? bn : tv);
-      tile.out_col0 = f * 128;
-      tiles[base + f * tt + t] = tile;
+  const int total = tiles_sc[1023];
+  if (s == 0) *lists.count[blockIdx.x] = total;
+  for (int j = s; j < total; j += 1024) {
+    int lo = 0, hi = n_seg - 1;  // first segment whose inclusive tile sum exceeds j
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (tiles_sc[mid] > j) hi = mid;
+      else lo = mid + 1;
     }
+    const int seg = lo;
+    const int rows = seg_rows[seg];
+    const int tt = (rows + bn - 1) / bn;
+    const int local = j - (tiles_sc[seg] - ft * tt);
+    const int f = local / tt, t = local - f * tt;
+    const int e = seg_expert ? seg_expert[seg] : seg;
+    TcTile tile;
+    tile.w_row = e * n_out + f * 128;
+    tile.x_row = rows_sc[seg] - rows + t * bn;
+    const int fv = n_out - f * 128, tv = rows - t * bn;
+    tile.valid = ((fv > 128 ? 128 : fv) << 16) | (tv > bn ? bn : tv);
+    tile.out_col0 = f * 128;
+    tiles[j] = tile;
+  }
 }
 
 // Xp[pos, :] = x[perm[pos] / top_k, :]  (16-byte vectors; H % 8 == 0).
@@ -383,10 +402,14 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   int *err = device_error_ptr();
   const int64_t E = L.experts, H = L.hidden, I = L.inter;
   const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
-  build_tiles_kernel<<<1, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, (int)I, kMoeBN,
-                                        ws.tiles_up, ws.tile_counts);
-  build_tiles_kernel<<<1, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, (int)H, kMoeBN,
-                                        ws.tiles_down, ws.tile_counts + 1);
+  TileLists lists;
+  lists.n_out[0] = (int)I;
+  lists.n_out[1] = (int)H;
+  lists.tiles[0] = ws.tiles_up;
+  lists.tiles[1] = ws.tiles_down;
+  lists.count[0] = ws.tile_counts;
+  lists.count[1] = ws.tile_counts + 1;
+  build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, lists);
   nk_status st = check_launch("build_tiles_kernel");
   if (st != NK_OK) return st;
   if (R == 0) return NK_OK;

@@ -131,10 +131,17 @@ __global__ void plan_scan_kernel(int32_t *__restrict__ chunk_counts, int nchunks
   const int e = threadIdx.x;
   int32_t total = 0;
   if (e < E) {
-    for (int c = 0; c < nchunks; ++c) {
-      int32_t v = chunk_counts[(int64_t)c * E + e];
-      chunk_counts[(int64_t)c * E + e] = total;  // becomes the chunk's base for expert e
-      total += v;
+    for (int c0 = 0; c0 < nchunks; c0 += 8) {  // 8 loads in flight, then the running sum
+      int32_t v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = c0 + j < nchunks ? chunk_counts[(int64_t)(c0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < nchunks) {
+          chunk_counts[(int64_t)(c0 + j) * E + e] = total;  // the chunk's base for expert e
+          total += v[j];
+        }
     }
     counts[e] = total;
   }
@@ -160,21 +167,29 @@ __global__ void plan_place_kernel(const int32_t *__restrict__ idx, int64_t slots
     run[e] = offsets[e] + chunk_base[(int64_t)blockIdx.x * E + e];
   __syncwarp();
   int64_t base = (int64_t)blockIdx.x * kPlanChunk;
-  for (int g = 0; g < kPlanChunk; g += 32) {
-    int64_t s = base + g + lane;
-    bool valid = s < slots;
-    int e = valid ? idx[s] : -1 - lane;  // unique negative keys for idle lanes
-    if (valid && (e < 0 || e >= E)) e = -100 - lane;
-    unsigned peers = __match_any_sync(0xffffffffu, e);
-    int rank = __popc(peers & ((1u << lane) - 1));
-    if (valid && e >= 0) {
-      int pos = run[e] + rank;
-      perm[pos] = (int32_t)s;
-      slot_pos[s] = pos;
+  for (int g0 = 0; g0 < kPlanChunk; g0 += 32 * 8) {  // 8 loads per lane in flight
+    int ev[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t s = base + g0 + j * 32 + lane;
+      ev[j] = s < slots ? idx[s] : -1;
     }
-    __syncwarp();
-    if (valid && e >= 0 && rank == 0) run[e] += __popc(peers);
-    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t s = base + g0 + j * 32 + lane;
+      const bool valid = s < slots && ev[j] >= 0 && ev[j] < E;
+      const int e = valid ? ev[j] : -1 - lane;  // unique negative keys for idle lanes
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(peers & ((1u << lane) - 1));
+      if (valid) {
+        const int pos = run[e] + rank;
+        perm[pos] = (int32_t)s;
+        slot_pos[s] = pos;
+      }
+      __syncwarp();
+      if (valid && rank == 0) run[e] += __popc(peers);
+      __syncwarp();
+    }
   }
 }
 

@@ -71,7 +71,9 @@ def test_route_nan_and_inf(cuda):
 
 def test_plan_bit_exact(cuda):
     r = rng(9)
-    for (t, k, e) in [(4096, 6, 128), (1, 2, 4), (3000, 8, 1000), (10, 3, 3)]:
+    # several chunks of 1024 routes, a partial chunk, wide expert counts
+    for (t, k, e) in [(4096, 6, 128), (1, 2, 4), (3000, 8, 1000), (10, 3, 3),
+                      (16384, 4, 256), (20000, 4, 128), (500, 2, 257)]:
         idx = r.integers(0, e, size=t * k).astype(np.int32)
         idx[: t * k // 3] = 0  # a hot expert
         counts_ref, offs_ref, perm_ref = orc.route_histogram(idx, t, k, e)
