@@ -48,7 +48,7 @@ __device__ __forceinline__ uint32_t mma_n(int t_valid, int bn) {
 template <int WK, int BN, int PAIR>
 __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
-                   const __grid_constant__ CUtensorMap xmap, const TcArgs args) {
+                   const __grid_constant__ TokenMaps xmaps, const TcArgs args) {
   using Cfg = TcConfig<WK, BN, PAIR>;
   constexpr int S = Cfg::kStages;
   constexpr int FH = Cfg::kFeatRows;
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
     abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&wmap);
-    tma_prefetch_desc(&xmap);
+    for (int i = 0; i < kTokenBoxes && (16 << i) <= BN; ++i) tma_prefetch_desc(&xmaps.m[i]);
   }
   if (warp == 1) {
     if (PAIR == 2) {
@@ -134,6 +134,12 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         const uint32_t n_mma = mma_n(tile.valid & 0xFFFF, BN);
         const int a_row = tile.w_row + (int)rank * 128;
         const int b_row = tile.x_row + (int)rank * (int)(n_mma / PAIR);
+        uint32_t x_box = 16;  // single CTAs: the smallest token box covering n_mma rows
+        int x_map = 0;
+        while (PAIR == 1 && x_box < n_mma) {
+          x_box <<= 1;
+          ++x_map;
+        }
         for (int kk = 0; kk < k_count; ++kk) {
           if (*abort_v || !mbar_wait(&empty[stage], phase ^ 1, err)) {
             ok = false;
@@ -146,7 +152,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
           // quantized raw weight tiles complete on this CTA's `rawfull`.
           if (leader)
             mbar_arrive_expect_tx(&full[stage],
-                                  PAIR * ((kQuant ? 0 : Cfg::kABytes) + Cfg::kBBytes));
+                                  PAIR * ((kQuant ? 0 : Cfg::kABytes) +
+                                          (PAIR == 2 ? Cfg::kBBytes : x_box * 128)));
           if (kQuant) {
             mbar_arrive_expect_tx(&rawfull[stage], Cfg::kRawBytes);
             if (WK == WK_INT8)
@@ -160,11 +167,12 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
             const uint32_t fb = leader_bar(&full[stage]);
             if (!kQuant)
               tma_load_2d_pair(a_tiles + stage * Cfg::kABytes, &wmap, fb, wkb * 64, a_row);
-            tma_load_2d_pair(b_tiles + stage * Cfg::kBBytes, &xmap, fb, xkb * 64, b_row);
+            tma_load_2d_pair(b_tiles + stage * Cfg::kBBytes, &xmaps.m[0], fb, xkb * 64, b_row);
           } else {
             if (!kQuant)
               tma_load_2d(a_tiles + stage * Cfg::kABytes, &wmap, &full[stage], wkb * 64, a_row);
-            tma_load_2d(b_tiles + stage * Cfg::kBBytes, &xmap, &full[stage], xkb * 64, b_row);
+            tma_load_2d(b_tiles + stage * Cfg::kBBytes, &xmaps.m[x_map], &full[stage], xkb * 64,
+                        b_row);
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -460,7 +468,7 @@ nk_status make_map(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes, con
 }
 
 template <int WK, int BN, int PAIR>
-nk_status launch_impl(const CUtensorMap &wm, const CUtensorMap &xm, const TcArgs &args, int grid,
+nk_status launch_impl(const CUtensorMap &wm, const TokenMaps &xm, const TcArgs &args, int grid,
                       cudaStream_t stream) {
   using Cfg = TcConfig<WK, BN, PAIR>;
   static bool attr_done = false;  // benign race: setting the attribute twice is harmless
@@ -491,7 +499,7 @@ nk_status launch_impl(const CUtensorMap &wm, const CUtensorMap &xm, const TcArgs
 }
 
 template <int WK>
-nk_status launch_kind(int bn, int pair, const CUtensorMap &wm, const CUtensorMap &xm,
+nk_status launch_kind(int bn, int pair, const CUtensorMap &wm, const TokenMaps &xm,
                       const TcArgs &args, int grid, cudaStream_t stream) {
   if (pair == 2) return launch_impl<WK, 256, 2>(wm, xm, args, grid, stream);
   return bn == 256 ? launch_impl<WK, 256, 1>(wm, xm, args, grid, stream)
@@ -506,7 +514,7 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
                   TcArgs args, int grid, cudaStream_t stream, int pair) {
   if (pair == 2 && (bn != 256 || (grid & 1)))
     return fail(NK_UNSUPPORTED, "CTA pairs need 256-token tiles and an even grid");
-  CUtensorMap wm, xm;
+  CUtensorMap wm;
   nk_status st;
   if (wk == WK_BF16)
     st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, (uint64_t)w_k, (uint64_t)w_rows,
@@ -518,9 +526,18 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
     st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)(w_rows / 2),
                   (uint64_t)w_k, (uint64_t)ldw_bytes, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != NK_OK) return st;
-  st = make_map(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)x_k, (uint64_t)x_rows,
-                (uint64_t)ldx_elems * 2, 64, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != NK_OK) return st;
+  TokenMaps xm;
+  for (int i = 0; i < kTokenBoxes; ++i) {
+    const int box = pair == 2 ? bn / 2 : 16 << i;
+    if (box > bn || (pair == 2 && i > 0)) {
+      xm.m[i] = xm.m[0];  // unused slot
+      continue;
+    }
+    st = make_map(&xm.m[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)x_k,
+                  (uint64_t)x_rows, (uint64_t)ldx_elems * 2, 64, (uint32_t)box,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != NK_OK) return st;
+  }
   if (grid <= 0) return ok();
   if (wk == WK_BF16) return launch_kind<WK_BF16>(bn, pair, wm, xm, args, grid, stream);
   if (wk == WK_INT8) return launch_kind<WK_INT8>(bn, pair, wm, xm, args, grid, stream);

@@ -61,6 +61,16 @@ struct TcArgs {
   int *err;
 };
 
+// Activation tensor maps with token boxes of 16, 32, 64, 128 and 256 rows
+// (boxes above the tile's BN unused): each stage loads the token rows with
+// ONE TMA copy of the smallest box that covers the rows the MMA reads, so a
+// decode tile of a few tokens does not move a full BN-row tile.  CTA pairs
+// use m[0] only (a BN/2-row box per CTA).
+constexpr int kTokenBoxes = 5;
+struct TokenMaps {
+  CUtensorMap m[kTokenBoxes];
+};
+
 template <int WK>
 struct WeightTile {
   static constexpr int kRawBytes = WK == WK_BF16 ? 0 : (WK == WK_INT8 ? 128 * 64 : 64 * 64);
