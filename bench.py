@@ -498,6 +498,12 @@ def reference_arm(args):
     secs = [cpu_sample(wnp, x, n_tok, min(threads, n_tok), orc) for _ in range(args.steps)]
     total = sum(secs)
     value = n_tok * args.steps / total
+    # MoeLayer::forward_into as written runs every selected expert over all T
+    # rows (moe.rs:195-246): with all 128 experts selected at T = 4096 that is
+    # E·T row-MLPs instead of the T·k gathered ones.  Its rate, scaled by the
+    # FLOP ratio from the gathered timing above:
+    routed, shared, router = layer_flops(T)
+    dense_ratio = (routed * E / K + shared + router) / (routed + shared + router)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -508,7 +514,12 @@ def reference_arm(args):
                          "kind": "port",
                          "sample": f"{n_tok} of {T} tokens per step, the reference's MoE host "
                                    "algorithm (oracle/nk_oracle.c, gathered rows) over "
-                                   f"{min(threads, n_tok)} threads"},
+                                   f"{min(threads, n_tok)} threads",
+                         "as_written_estimate": {
+                             "value": value / dense_ratio, "unit": "tokens/s",
+                             "note": "every selected expert over all tokens, as moe.rs:195-246 "
+                                     f"computes it: the gathered rate / {dense_ratio:.1f} "
+                                     "(FLOP ratio), not timed"}},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -598,7 +609,7 @@ def nk_arm(args):
     barrier()
 
     # With --graph the step replays a CUDA graph captured from the C-ABI call
-    # (the 14 kernel launches of one forward), stage-timing events included.
+    # (the 13 kernel launches of one forward), stage-timing events included.
     if args.graph and world == 1:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -733,7 +744,11 @@ def nk_arm(args):
             "e2e": {"value": tokens_total / (total_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
             "clocks": clocks,
-            "gpu_launches": 14 * args.steps * 2,
+            # libnk launches per forward: one GPU 13 (router GEMM + reduce, route,
+            # plan count / scan / place, gather, tile lists, up, down, shared up /
+            # down, combine); expert-parallel 15 (no gather; exchange plan,
+            # dispatch and return instead)
+            "gpu_launches": (13 if world == 1 else 15) * args.steps * 2,
         }
         line["config"]["e2e"] = (
             "nk_moe_pipeline_submit per step (host-buffer executor: pinned x in, f32 out back; "
