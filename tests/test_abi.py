@@ -113,6 +113,26 @@ def test_moe_layer_validation():
                               None) == nk.WORKSPACE_TOO_SMALL
 
 
+def test_moe_pipeline_validation():
+    # nk_moe_pipeline_*: argument checks come before any device call.
+    lib = nk.lib()
+    s = nk.NkMoeLayer()
+    s.hidden, s.experts, s.top_k, s.inter = 8, 2, 1, 16
+    s.router_w3 = s.up_w = s.down_w = 16
+    p = ctypes.c_void_p()
+    assert lib.nk_moe_pipeline_create(None, 4, nk.F32, None, None, None, ctypes.byref(p)) == nk.INVALID_PARAMS
+    assert lib.nk_moe_pipeline_create(ctypes.byref(s), 0, nk.F32, None, None, None,
+                                      ctypes.byref(p)) == nk.INVALID_ROW_COUNT
+    assert lib.nk_moe_pipeline_create(ctypes.byref(s), 4, 9, None, None, None,
+                                      ctypes.byref(p)) == nk.UNSUPPORTED
+    assert lib.nk_moe_pipeline_create(ctypes.byref(s), 4, nk.F32, 16, None, None,
+                                      ctypes.byref(p)) == nk.INVALID_PARAMS  # some streams, not all
+    assert p.value is None
+    assert lib.nk_moe_pipeline_submit(None, None, 4, None, None) == nk.INVALID_PARAMS
+    assert lib.nk_moe_pipeline_wait(None) == nk.INVALID_PARAMS
+    assert lib.nk_moe_pipeline_destroy(None) == nk.OK
+
+
 def test_mamba_glue_validation_order():
     lib = nk.lib()
     # conv1d.rs:126-158: shape, then input, weights, output lengths
