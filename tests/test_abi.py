@@ -120,7 +120,8 @@ def test_moe_pipeline_validation():
     s.hidden, s.experts, s.top_k, s.inter = 8, 2, 1, 16
     s.router_w3 = s.up_w = s.down_w = 16
     p = ctypes.c_void_p()
-    assert lib.nk_moe_pipeline_create(None, 4, nk.F32, None, None, None, ctypes.byref(p)) == nk.INVALID_PARAMS
+    assert lib.nk_moe_pipeline_create(None, 4, nk.F32, None, None, None,
+                                      ctypes.byref(p)) == nk.INVALID_PARAMS
     assert lib.nk_moe_pipeline_create(ctypes.byref(s), 0, nk.F32, None, None, None,
                                       ctypes.byref(p)) == nk.INVALID_ROW_COUNT
     assert lib.nk_moe_pipeline_create(ctypes.byref(s), 4, 9, None, None, None,
