@@ -61,12 +61,13 @@ struct TcArgs {
   int *err;
 };
 
-// Activation tensor maps with token boxes of 16, 32, 64, 128 and 256 rows
+// Activation tensor maps with token boxes of 16, 32, 64, 96, ..., 256 rows
 // (boxes above the tile's BN unused): each stage loads the token rows with
 // ONE TMA copy of the smallest box that covers the rows the MMA reads, so a
-// decode tile of a few tokens does not move a full BN-row tile.  CTA pairs
-// use m[0] only (a BN/2-row box per CTA).
-constexpr int kTokenBoxes = 5;
+// decode tile of a few tokens, or an expert's 192 routed rows, does not move
+// a full BN-row tile.  CTA pairs use m[0] only (a BN/2-row box per CTA).
+constexpr int kTokenBoxes = 9;
+__host__ __device__ constexpr int token_box_rows(int i) { return i < 2 ? 16 << i : 32 * i; }
 struct TokenMaps {
   CUtensorMap m[kTokenBoxes];
 };
