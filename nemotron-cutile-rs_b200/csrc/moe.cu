@@ -114,6 +114,12 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16 *__res
   __syncthreads();
   const int64_t vecs = H >> 3;
   for (int64_t v = threadIdx.x; v < vecs; v += blockDim.x) {
+    // all rows' vectors are requested before the rank-ordered sums use them
+    // (up to 8 in flight; larger top_k continues one row at a time)
+    uint4 yv[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < top_k) yv[r] = reinterpret_cast<const uint4 *>(y + (int64_t)pos[r] * H)[v];
     float o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = 0.0f;
@@ -123,7 +129,15 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16 *__res
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(o[i], sf[i]);
     }
-    for (int r = 0; r < top_k; ++r) {
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r >= top_k) break;
+      float yf[8];
+      bf16x8_to_f32(yv[r], yf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(o[i], __fmul_rn(wt[r], yf[i]));
+    }
+    for (int r = 8; r < top_k; ++r) {
       float yf[8];
       bf16x8_to_f32(reinterpret_cast<const uint4 *>(y + (int64_t)pos[r] * H)[v], yf);
 #pragma unroll
