@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 128 * PAIR);
+      mbar_init(&conv[s], Cfg::kTransformThreads * PAIR);
       mbar_init(&rawfull[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
     }
   } else if (kQuant) {
     // ------------------------------------------------------------ transform
-    const int tid = threadIdx.x - 192;  // 0..127
+    const int tid = threadIdx.x - 192;  // 0 .. kTransformThreads-1
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -341,8 +341,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         const uint8_t *raw = raw_tiles + stage * Cfg::kRawBytes;
         uint8_t *dst = a_tiles + stage * Cfg::kABytes;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int idx = q * 128 + tid;
+        for (int q = 0; q < 1024 / Cfg::kTransformThreads; ++q) {
+          const int idx = q * Cfg::kTransformThreads + tid;
           int row, c;
           uint32_t packed[4];
           if (WK == WK_INT8) {

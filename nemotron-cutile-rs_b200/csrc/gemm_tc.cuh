@@ -16,7 +16,7 @@
 //   warp 0      TMA producer (one lane)
 //   warp 1      TMEM allocator + MMA issuer (one lane)
 //   warps 2-5   epilogue: TMEM -> registers -> scale/bias/relu2/token weight -> global
-//   warps 6-9   transform (quantized weights only)
+//   warps 6-13  transform (quantized weights only)
 // Every mbarrier wait is bounded (mbar_wait); on a timeout the kernel records
 // NK_TIMEOUT, drains its own TMA loads and MMAs, frees TMEM and returns.
 #pragma once
@@ -92,7 +92,11 @@ struct TcConfig {
 #define NK_STAGES_MAX 8
 #endif
   static constexpr int kStages = kStages0 > NK_STAGES_MAX ? NK_STAGES_MAX : kStages0;
-  static constexpr int kThreads = WK == WK_BF16 ? 192 : 320;
+#ifndef NK_TRANSFORM_THREADS
+#define NK_TRANSFORM_THREADS 256
+#endif
+  static constexpr int kTransformThreads = WK == WK_BF16 ? 0 : NK_TRANSFORM_THREADS;
+  static constexpr int kThreads = 192 + kTransformThreads;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
   static constexpr int kFeatRows = 128 * PAIR;      // features per output tile
