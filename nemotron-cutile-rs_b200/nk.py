@@ -441,12 +441,20 @@ class MoePipeline:
         self._h = h
 
     def submit(self, x_host, out_host, indices_host=None):
+        import torch
+
         for t in (x_host, out_host, indices_host):
             if t is not None and (t.is_cuda or not t.is_contiguous()):
                 raise ValueError("host tensors must be contiguous CPU tensors")
+        hidden, top_k = self.layer.weights.hidden, self.layer.weights.top_k
+        if x_host.dtype != torch.bfloat16 or x_host.dim() != 2 or x_host.shape[1] != hidden:
+            raise ValueError(f"x_host must be bf16 [tokens, {hidden}]")
         tokens = x_host.shape[0]
-        if out_host.dtype != self.out_dtype or out_host.numel() < tokens * self.layer.weights.hidden:
+        if out_host.dtype != self.out_dtype or out_host.numel() < tokens * hidden:
             raise ValueError("out_host must hold tokens x hidden values of the pipeline's dtype")
+        if indices_host is not None and (indices_host.dtype != torch.int32 or
+                                         indices_host.numel() < tokens * top_k):
+            raise ValueError("indices_host must hold tokens x top_k int32 values")
         call("nk_moe_pipeline_submit", self._h, x_host.data_ptr(), tokens, out_host.data_ptr(),
              None if indices_host is None else indices_host.data_ptr())
 
