@@ -59,6 +59,21 @@ void release(nk_moe_pipeline *p) {
   delete p;
 }
 
+// Makes the executor's device current for the scope of a call and restores
+// the caller's afterwards.
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceScope(int dev) {
+    err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 }  // namespace
 }  // namespace nk
 
@@ -125,6 +140,8 @@ nk_status nk_moe_pipeline_submit(nk_moe_pipeline *p, const uint16_t *x_host, int
   if (tokens <= 0) return fail(NK_INVALID_ROW_COUNT, "row_count must be non-zero");
   if (tokens > p->max_tokens) return fail(NK_UNSUPPORTED, "tokens exceeds the pipeline's max_tokens");
   if (!x_host || !out_host) return fail(NK_INVALID_PARAMS, "x_host and out_host must not be NULL");
+  DeviceScope dev(p->device);
+  if (dev.err != cudaSuccess) return fail_cuda(dev.err, "nk_moe_pipeline_submit");
   const int s = (int)(p->submitted & 1);
   const bool reuse = p->submitted >= 2;  // slot s last served submission - 2
   const size_t x_bytes = (size_t)tokens * p->layer.hidden * 2;
@@ -155,6 +172,8 @@ nk_status nk_moe_pipeline_submit(nk_moe_pipeline *p, const uint16_t *x_host, int
 
 nk_status nk_moe_pipeline_wait(nk_moe_pipeline *p) {
   if (!p) return fail(NK_INVALID_PARAMS, "pipeline must not be NULL");
+  DeviceScope dev(p->device);
+  if (dev.err != cudaSuccess) return fail_cuda(dev.err, "nk_moe_pipeline_wait");
   NK_CUDA_TRY(cudaStreamSynchronize(p->h2d));
   NK_CUDA_TRY(cudaStreamSynchronize(p->compute));
   NK_CUDA_TRY(cudaStreamSynchronize(p->d2h));
@@ -163,6 +182,7 @@ nk_status nk_moe_pipeline_wait(nk_moe_pipeline *p) {
 
 nk_status nk_moe_pipeline_destroy(nk_moe_pipeline *p) {
   if (!p) return ok();
+  DeviceScope dev(p->device);
   cudaStreamSynchronize(p->h2d);
   cudaStreamSynchronize(p->compute);
   cudaStreamSynchronize(p->d2h);
