@@ -1,4 +1,4 @@
-"""Expert-parallel orchestration (nk_ep.ExpertParallelMoe) on 2 gloo ranks on
+"""Expert-parallel orchestration (nk_ep.ExpertParallelMoe) on 2 and 4 gloo ranks on
 CPU, with the oracle as compute backend: sharding the experts over ranks and
 exchanging routed rows must reproduce the single-process MoeLayer::forward_into
 (moe.rs:154-249) on each rank's tokens bit for bit."""
@@ -54,12 +54,16 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("tokens,mode", [((37, 21), 0), ((5, 64), 2), ((1, 1), 1)])
-def test_ep_two_ranks_matches_single_process(tokens, mode):
+@pytest.mark.parametrize("tokens,mode", [((37, 21), 0), ((5, 64), 2), ((1, 1), 1),
+                                         ((9, 1, 30, 4), 2)])
+def test_ep_ranks_match_single_process(tokens, mode):
+    # 2 ranks (4 experts each) and 4 ranks (2 experts each, ragged token counts)
+    world = len(tokens)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, tokens, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, mode, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in procs]

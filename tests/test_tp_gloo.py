@@ -1,4 +1,4 @@
-"""Tensor-parallel projections (nk_tp) on 2 gloo ranks on CPU, with the
+"""Tensor-parallel projections (nk_tp) on 2 and 4 gloo ranks on CPU, with the
 oracle's LinearProjection restatement (linear.rs:283-342) standing in for the
 device GEMM: a column-parallel up projection (relu2) followed by a
 row-parallel down projection must reproduce the single-process MLP
@@ -54,21 +54,23 @@ def _worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_tp_two_ranks_matches_single_process_mlp():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_ranks_match_single_process_mlp(world):
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert res[0][2] == (0, I // 2) and res[1][2] == (I // 2, I)
-    assert res[0][3] == (0, I // 2) and res[1][3] == (I // 2, I)
-    for rank, err, _, _ in res:
+    part = I // world
+    for rank, err, cols, k_range in res:
+        assert cols == (rank * part, (rank + 1) * part)
+        assert k_range == (rank * part, (rank + 1) * part)
         assert err <= 1e-6, (rank, err)
