@@ -80,6 +80,13 @@ int32_t nk_version(void);
  * bounded wait gave up), then clears it. */
 nk_status nk_device_status(void *stream);
 
+/* Failure-detection self test: launches one kernel whose bounded device-side
+ * wait (the kind every libnk kernel uses on its barriers) runs out after
+ * about 2 s because nothing completes it; the kernel records NK_TIMEOUT and
+ * returns, so the next nk_device_status(stream) reports NK_TIMEOUT (and
+ * clears it) and the context stays usable.  No fault, trap or hang. */
+nk_status nk_selftest_wait_timeout(void *stream);
+
 /* dtypes of activations / outputs */
 enum { NK_F32 = 0, NK_BF16 = 1 };
 /* epilogue flags */

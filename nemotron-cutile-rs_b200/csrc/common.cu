@@ -4,8 +4,21 @@
 #include <vector>
 
 #include "nk_common.cuh"
+#include "nk_ptx.cuh"
 
 namespace nk {
+
+// One thread waits on an mbarrier phase that nothing completes: the bounded
+// wait every libnk kernel uses gives up after NK_WAIT_LIMIT_NS and records
+// NK_TIMEOUT in the device error word, and the kernel returns.
+__global__ void wait_selftest_kernel(int *err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0, err);
+  }
+}
 
 nk_error_info &tls_error() {
   static thread_local nk_error_info e{};
@@ -85,6 +98,13 @@ nk_status nk_last_error(nk_error_info *out) {
 }
 
 int32_t nk_version(void) { return 100; }
+
+nk_status nk_selftest_wait_timeout(void *stream) {
+  int *err = nk::device_error_ptr();
+  if (!err) return nk::fail(NK_DEVICE_ERROR, "cannot resolve device error word");
+  nk::wait_selftest_kernel<<<1, 32, 0, nk::as_stream(stream)>>>(err);
+  return nk::check_launch("wait_selftest_kernel");
+}
 
 nk_status nk_device_status(void *stream) {
   NK_CUDA_TRY(cudaStreamSynchronize(nk::as_stream(stream)));

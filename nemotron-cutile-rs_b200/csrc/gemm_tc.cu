@@ -340,9 +340,10 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         }
         const uint8_t *raw = raw_tiles + stage * Cfg::kRawBytes;
         uint8_t *dst = a_tiles + stage * Cfg::kABytes;
+        constexpr int kTT = Cfg::kTransformThreads > 0 ? Cfg::kTransformThreads : 1;
 #pragma unroll
-        for (int q = 0; q < 1024 / Cfg::kTransformThreads; ++q) {
-          const int idx = q * Cfg::kTransformThreads + tid;
+        for (int q = 0; q < 1024 / kTT; ++q) {
+          const int idx = q * kTT + tid;
           int row, c;
           uint32_t packed[4];
           if (WK == WK_INT8) {

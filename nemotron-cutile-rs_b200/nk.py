@@ -131,6 +131,7 @@ _SIGS = {
     "nk_linear_pack_kn": (_i32, [_p, _i64, _i64, _p, _p]),
     "nk_moe_workspace_bytes": (_i32, [_p, _i64, _p]),
     "nk_moe_forward": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+    "nk_selftest_wait_timeout": (_i32, [_p]),
     "nk_moe_pipeline_create": (_i32, [_p, _i64, _i32, _p, _p, _p, _p]),
     "nk_moe_pipeline_submit": (_i32, [_p, _p, _i64, _p, _p]),
     "nk_moe_pipeline_wait": (_i32, [_p]),
