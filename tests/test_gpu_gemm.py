@@ -115,6 +115,21 @@ def test_gemm_int8_row(cuda, m, k, n):
         assert rel_err(host(y), ref) <= FP32_TOL, xdt
 
 
+def test_config1_int8_linear_full_size(cuda):
+    """BASELINE config 1 at its own size and seed: X f32 [64, 2048] ~ N(0,1),
+    W f32 [2048, 2048] ~ N(0, 0.02), int8 per-row absmax quantization (bytes
+    and scales bit-exact), Y = X·dequant(W)ᵀ within the f32-accumulate bar."""
+    r = rng(0)
+    x = r.standard_normal((64, 2048)).astype(np.float32)
+    w = (r.standard_normal((2048, 2048)) * 0.02).astype(np.float32)
+    q_ref, s_ref = orc.quantize_int8_row(w)
+    q, s = nk.quantize_int8_row(dev(w))
+    assert np.array_equal(host(q), q_ref) and np.array_equal(host(s), s_ref)
+    ref = _oracle_proj(x, q_ref.astype(np.float32) * s_ref[:, None])
+    y = nk.gemm(dev(x), q, kind="int8", scales=s)
+    assert rel_err(host(y), ref) <= FP32_TOL
+
+
 @pytest.mark.parametrize("m,k,n", [(64, 2048, 256), (1, 256, 64), (200, 128, 96), (3, 40, 10)])
 def test_gemm_int4_reference_layout(cuda, m, k, n):
     """Linear with INT4-affine weights in the reference [K,N] layout, dequantized in-kernel."""
