@@ -1,4 +1,4 @@
-"""bench.py — MoE layer throughput through libnk on B200.
+"""bench.py — MoE layer throughput (benchmark config 3) through libnk on B200.
 
 A step is one MoeLayer forward (router GEMM -> top-6 routing -> grouped expert
 GEMMs -> shared expert -> combine) over T=4096 tokens per GPU, hidden 2688,
@@ -203,7 +203,7 @@ class L2Flush:
 
 
 def gemm_sweep(torch, nk, dev, reps=5):
-    """Y = X·Wᵀ, bf16 and int8-per-row weights, per shape the
+    """Benchmark config 2: Y = X·Wᵀ, bf16 and int8-per-row weights, per shape the
     mean of `reps` CUDA-event timings of a graph replay with an L2 flush before
     each; cuBLAS (torch.matmul, bf16) timed the same way for context."""
     pk = peaks()
@@ -255,7 +255,7 @@ def gemm_sweep(torch, nk, dev, reps=5):
 
 
 def tp_projections(torch, dev, world, reps=10):
-    """BASELINE config 4's GEMMs at T=8192: Mamba2 in_proj [4096 -> 18560]
+    """Benchmark config 4's GEMMs at T=8192: Mamba2 in_proj [4096 -> 18560]
     column-parallel and out_proj [8192 -> 4096] row-parallel with one NCCL
     all-reduce of f32 partials, over the `world` ranks (strong scaling)."""
     import torch.distributed as dist
@@ -372,7 +372,7 @@ def mamba_block(torch, dev, world, w_in, w_out, x, reps):
 
 
 def decoder_e2e(torch, dev, batch=64, prompt_len=1024, gen=256):
-    """the random-initialised 52-layer hybrid decoder
+    """Benchmark config 5: the random-initialised 52-layer hybrid decoder
     (23 Mamba2, 23 MoE as config 3, 6 GQA attention; hidden 2688, vocab
     131072) on one GPU: prefill `batch` prompts of `prompt_len` random ids,
     then greedy-decode `gen` tokens per sequence reusing the KV / conv / SSM
@@ -528,7 +528,7 @@ def reference_arm(args):
 
 
 def config_dict(args, impl):
-    return {"workload": "MoE layer prefill (BASELINE config 3)", "tokens_per_gpu": T,
+    return {"workload": "MoE layer prefill (benchmark config 3)", "tokens_per_gpu": T,
             "hidden": H, "experts": E, "top_k": K, "expert_inter": I, "shared_inter": IS,
             "routing": "sigmoid top-6 renormalised", "weights": args.weights,
             "parallelism": (f"expert-parallel x{args.gpus}: {E // max(args.gpus, 1)} experts per "

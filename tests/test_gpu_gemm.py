@@ -116,7 +116,7 @@ def test_gemm_int8_row(cuda, m, k, n):
 
 
 def test_config1_int8_linear_full_size(cuda):
-    """BASELINE config 1 at its own size and seed: X f32 [64, 2048] ~ N(0,1),
+    """Benchmark config 1 at its own size and seed: X f32 [64, 2048] ~ N(0,1),
     W f32 [2048, 2048] ~ N(0, 0.02), int8 per-row absmax quantization (bytes
     and scales bit-exact), Y = X·dequant(W)ᵀ within the f32-accumulate bar."""
     r = rng(0)
