@@ -160,18 +160,6 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16 *__res
   }
 }
 
-// scores[i] = (Σ_s partial[s][i]) + bias[i % E], partial sums added in split order.
-__global__ void router_reduce_kernel(const float *__restrict__ partial, int splits, int64_t n,
-                                     int E, const float *__restrict__ bias,
-                                     float *__restrict__ scores) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float acc = partial[i];
-  for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, partial[(int64_t)s * n + i]);
-  if (bias) acc = __fadd_rn(acc, bias[i % E]);
-  scores[i] = acc;
-}
-
 namespace {
 
 constexpr int kStages = 7;
@@ -212,14 +200,15 @@ struct Carver {
 
 // Scratch of the dispatch stage (router, routing, plan, gather).
 struct DispatchWs {
-  float *scores, *router_partial;
+  float *router_partial;
+  void *route_scratch;
   int32_t *perm, *plan_scratch;
 };
 DispatchWs carve_dispatch(const nk_moe_layer &L, int64_t T, Carver &c) {
   const int64_t E = L.experts, S = T * L.top_k;
   DispatchWs w;
-  w.scores = (float *)c.take(sizeof(float) * T * E);
   w.router_partial = (float *)c.take(sizeof(float) * T * E * kRouterMaxSplits);
+  w.route_scratch = c.take(route_exact_scratch_bytes(T, E));
   w.perm = (int32_t *)c.take(sizeof(int32_t) * S);
   w.plan_scratch = (int32_t *)c.take(plan_scratch_bytes(S, E));
   return w;
@@ -355,13 +344,17 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
   const int64_t E = L.experts, K = L.top_k, H = L.hidden, S = T * K;
   nk_status st;
   tm.mark(0, s);
-  // router scores [T, E] f32: x · (hi + mid + lo)ᵀ.  K is split over CTAs into f32
-  // partial sums, reduced in split order; the bias is added after the GEMM as
-  // linear.rs:333-339 does.
+  // router scores [T, E] f32: x · (hi + mid)ᵀ.  K is split over CTAs into f32
+  // partial sums; the routing kernels add them in split order and add the bias
+  // after the GEMM as linear.rs:333-339 does.  These scores are approximate
+  // (tensor-core f32 accumulation); the routing rescores the experts near each
+  // token's top-k boundary exactly, given the accumulation bound c.
+  float c_bound = 0.0f;
+  int router_splits = 1;
   {
     const int64_t hp = ceil_div(H, 64) * 64;
     const int bn = T <= 64 ? 64 : 256;
-    const int k_blocks = (int)(3 * hp / 64);
+    const int k_blocks = (int)(2 * hp / 64);  // hi and mid parts; lo enters the bound
     TcArgs a = base_args(err);
     a.f_tiles = (int)ceil_div(E, 128);
     a.t_tiles = (int)ceil_div(T, bn);
@@ -383,16 +376,15 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
     a.y_f32 = 1;
     int64_t tiles = (int64_t)base_tiles * splits;
     int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    st = tc_gemm(WK_BF16, L.router_w3, E, 3 * hp, 3 * hp * 2, x, T, H, H, bn, a, grid, s);
+    st = tc_gemm(WK_BF16, L.router_w3, E, 2 * hp, 3 * hp * 2, x, T, H, H, bn, a, grid, s);
     if (st != NK_OK) return st;
-    const int64_t n = T * E;
-    router_reduce_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
-        ws.router_partial, splits, n, (int)E, L.router_b, ws.scores);
-    st = check_launch("router_reduce_kernel");
-    if (st != NK_OK) return st;
+    c_bound = (float)((double)(per * 64 + splits + 2) * 0x1p-22);
+    router_splits = splits;
   }
   tm.mark(1, s);
-  st = launch_route(ws.scores, T, (int)E, (int)K, L.route_mode, idx, rw, s);
+  st = launch_route_exact(ws.router_partial, router_splits, x, T, (int)H, L.router_w3,
+                          L.router_b, c_bound, (int)E, (int)K, L.route_mode, ws.route_scratch,
+                          idx, rw, s);
   if (st != NK_OK) return st;
   st = launch_plan(idx, S, (int)E, counts, offsets, ws.perm, slot_pos, ws.plan_scratch, s);
   if (st != NK_OK) return st;

@@ -1,9 +1,13 @@
 """MoE layer on the B200 (router -> top-k -> grouped expert GEMMs -> combine)
 against the oracle's MoeLayer::forward_into restatement (moe.rs:154-249).
-Outputs: max|y-r|/max|r| <= 2e-2 (bf16 activations).  Routing indices are
-compared slot by slot; the router scores come from a different (f32 tensor
-core vs f64) summation, so a token whose top-k boundary is a near tie may
-differ — those tokens are excluded from the output comparison and counted."""
+
+Routing indices and expert counts are bit-exact for every token: the
+tensor-core router's approximate scores only choose which experts to rescore,
+and those are rescored with the reference's sequential f64 sum
+(gemm.rs:99-109) before the top-k choice (moe_routing.rs:168-186).  Routing
+weights: |w - w_ref| <= 1e-6 (sigmoid evaluates exp in double rounded once on
+the device, libm expf in the oracle; they agree to the last ulp in practice).
+Outputs: max|y-r|/max|r| <= 2e-2 (bf16 activations)."""
 import numpy as np
 import pytest
 import torch
@@ -78,12 +82,10 @@ def test_moe_matches_oracle(cuda, kind, T, H, E, K, I, Is, mode, bias):
     nk.device_status()
     ref_out, ref_idx, ref_w = oracle_moe(ref, x, H, E, K, I, Is, mode)
     gi = host(idx).reshape(T, K)
-    same = np.all(gi == ref_idx.reshape(T, K), axis=1)
-    assert same.mean() >= 0.99, same.mean()
-    yo = host(y).reshape(T, H)[same]
-    ro = ref_out.reshape(T, H)[same]
-    assert rel_err(yo, ro) <= BF16_TOL
-    assert np.max(np.abs(host(rw).reshape(T, K)[same] - ref_w.reshape(T, K)[same])) <= 1e-4
+    mism = int(np.sum(np.any(gi != ref_idx.reshape(T, K), axis=1)))
+    assert mism == 0, f"{mism} of {T} tokens routed differently from the oracle"
+    assert rel_err(host(y).reshape(T, H), ref_out.reshape(T, H)) <= BF16_TOL
+    assert np.max(np.abs(host(rw).reshape(T, K) - ref_w.reshape(T, K))) <= 1e-6
 
 
 def test_moe_bf16_output_and_repeat_determinism(cuda):
@@ -132,3 +134,91 @@ def test_host_pipeline_matches_device_forward(cuda):
     with pytest.raises(nk.NkError):
         pipe.submit(torch.zeros(T + 1, H, dtype=torch.bfloat16), torch.zeros(T + 1, H))
     pipe.close()
+
+
+def test_config3_full_size_routing_and_sampled_output(cuda):
+    """Config 3 at its own size: T=4096, H=2688, 128 experts x 1856, shared
+    3712, sigmoid top-6 renormalised.  All 4096 tokens' indices, weights and
+    the per-expert counts against the oracle's router projection
+    (linear.rs:283-342, f64 sums) and routing; the layer output against the
+    oracle composition (shared expert first, then w·MLP_e in rank order,
+    moe.rs:195-246) on 64 sampled tokens."""
+    import os
+
+    T, H, E, K, I, Is = 4096, 2688, 128, 6, 1856, 3712
+    g = torch.Generator(device="cuda").manual_seed(3003)
+    x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    router_w = torch.randn(E, H, device="cuda", generator=g) * 0.02
+    up = (torch.randn(E, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    down = (torch.randn(E, H, I, device="cuda", generator=g) * 0.02).bfloat16()
+    sup = (torch.randn(Is, H, device="cuda", generator=g) * 0.02).bfloat16()
+    sdown = (torch.randn(H, Is, device="cuda", generator=g) * 0.02).bfloat16()
+    w = nk.MoeWeights(hidden=H, experts=E, top_k=K, inter=I, shared_inter=Is,
+                      route_mode=nk.ROUTE_SIGMOID_RENORM, weight_kind=nk.W_BF16,
+                      router_w3=nk.router_split(router_w), up_w=up, down_w=down,
+                      shared_up_w=sup, shared_down_w=sdown)
+    layer = nk.MoeLayer(w)
+    idx = torch.empty(T * K, dtype=torch.int32, device=cuda)
+    rw = torch.empty(T * K, dtype=torch.float32, device=cuda)
+    y = layer.forward(x, indices=idx, weights=rw)
+    nk.device_status()
+
+    xh = host(x)
+    rwh = host(router_w)
+    scores = orc.gemm_rows(xh, rwh.T.copy(), T, H, E, T, threads=os.cpu_count() or 1)
+    ref_idx, ref_w = orc.route(scores, T, E, K, orc.SIGMOID_RENORM)
+    gi, gw = host(idx), host(rw)
+    mism = int(np.sum(np.any(gi.reshape(T, K) != ref_idx.reshape(T, K), axis=1)))
+    assert mism == 0, f"{mism} of {T} tokens routed differently from the oracle"
+    assert np.max(np.abs(gw - ref_w)) <= 1e-6
+    counts, _, _ = orc.route_histogram(ref_idx, T, K, E)
+    gcounts = np.bincount(gi, minlength=E)
+    assert np.array_equal(gcounts, counts)
+
+    sample = np.sort(rng(7).choice(T, 64, replace=False))
+    xs = xh[sample]
+    ref_sh = orc.mlp(H, Is, host(sup).T.copy(), None, host(sdown).T.copy(), None, xs, len(sample))
+    ref_sh = ref_sh.reshape(len(sample), H)
+    ri = ref_idx.reshape(T, K)[sample]
+    rws = ref_w.reshape(T, K)[sample]
+    ye = np.zeros((len(sample), K, H), np.float32)
+    for e in np.unique(ri):
+        rows, ranks = np.nonzero(ri == e)
+        ue = host(up[e]).T.copy()      # reference layout [H, I]
+        de = host(down[e]).T.copy()    # [I, H]
+        ye[rows, ranks] = orc.mlp(H, I, ue, None, de, None, xs[rows], len(rows)).reshape(-1, H)
+    ref = np.float32(0.0) + ref_sh
+    for r in range(K):
+        ref = ref + rws[:, r:r + 1] * ye[:, r]
+    got = host(y)[sample]
+    assert rel_err(got, ref) <= BF16_TOL
+
+
+@pytest.mark.parametrize("scale", [0.02, 1.0])
+def test_moe_routing_ties_and_nan_tokens(cuda, scale):
+    """Router scores of order 16 (scale 1.0) saturate sigmoid at 1.0 in f32,
+    so many experts tie on weight and the reference breaks ties by index
+    (moe_routing.rs:177-181); a token with a NaN activation scores NaN on
+    every expert (NaN sorts above +inf under total_cmp).  Indices and weights
+    must still equal the oracle's; outputs are compared on the finite tokens."""
+    T, H, E, K, I, Is = 200, 256, 64, 6, 128, 0
+    w, ref = make_layer(17, H, E, K, I, Is, nk.ROUTE_SIGMOID, "bf16")
+    if scale != 0.02:
+        ref["router_w"] = (ref["router_w"] * (scale / 0.02)).astype(np.float32)
+        w.router_w3 = nk.router_split(dev(ref["router_w"]))
+    x = bf16_round(rng(5).standard_normal((T, H)))
+    x[3, 17] = np.nan
+    layer = nk.MoeLayer(w)
+    idx = torch.empty(T * K, dtype=torch.int32, device=cuda)
+    rw = torch.empty(T * K, dtype=torch.float32, device=cuda)
+    y = layer.forward(dev(x, torch.bfloat16), indices=idx, weights=rw)
+    nk.device_status()
+    ref_out, ref_idx, ref_w = oracle_moe(ref, x, H, E, K, I, Is, nk.ROUTE_SIGMOID)
+    assert np.array_equal(host(idx).reshape(T, K), ref_idx.reshape(T, K))
+    gw, rwr = host(rw).reshape(T, K), ref_w.reshape(T, K)
+    assert np.array_equal(np.isnan(gw), np.isnan(rwr))
+    fin = ~np.isnan(rwr)
+    assert np.max(np.abs(gw[fin] - rwr[fin])) <= 1e-6
+    ok_rows = np.all(np.isfinite(ref_out.reshape(T, H)), axis=1)
+    assert ok_rows.sum() == T - 1
+    assert rel_err(host(y).reshape(T, H)[ok_rows], ref_out.reshape(T, H)[ok_rows]) <= BF16_TOL
