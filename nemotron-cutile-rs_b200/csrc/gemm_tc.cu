@@ -2,6 +2,7 @@
 // and its host launcher.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -45,18 +46,20 @@ __device__ __forceinline__ uint32_t mma_n(int t_valid, int bn) {
   return n;
 }
 
-template <int WK, int BN, int PAIR>
-__global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
+template <int WK, int BN, int PAIR, int FA>
+__global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                    const __grid_constant__ TokenMaps xmaps, const TcArgs args) {
-  using Cfg = TcConfig<WK, BN, PAIR>;
+  using Cfg = TcConfig<WK, BN, PAIR, FA>;
+  constexpr int kSlots = Cfg::kAccSlots;
+  constexpr int kEpiWarps = Cfg::kEpiThreads / 32;
   constexpr int S = Cfg::kStages;
   constexpr int FH = Cfg::kFeatRows;
   constexpr bool kQuant = WK != WK_BF16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *a_tiles = smem;                          // S x 16 KB bf16 weight tiles (SW128)
+  uint8_t *a_tiles = smem;                          // S x FA x 16 KB bf16 weight tiles (SW128)
   uint8_t *b_tiles = a_tiles + S * Cfg::kABytes;    // S x kBRows*128 token tiles (SW128)
   uint8_t *raw_tiles = b_tiles + S * Cfg::kBBytes;  // S x raw weight tiles (quantized)
   uint64_t *bars = reinterpret_cast<uint64_t *>(raw_tiles + S * Cfg::kRawBytes);
@@ -64,8 +67,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
   uint64_t *empty = bars + S;       // MMAs finished reading the stage (every CTA)
   uint64_t *conv = bars + 2 * S;    // leader: converted weight tiles ready (both CTAs)
   uint64_t *rawfull = bars + 3 * S; // this CTA's raw weight tile landed (quantized)
-  uint64_t *tfull = bars + 4 * S;   // accumulator ready (2, every CTA)
-  uint64_t *tempty = tfull + 2;     // leader: accumulator drained (2)
+  uint64_t *tfull = bars + 4 * S;   // accumulator set ready (kSlots, every CTA)
+  uint64_t *tempty = tfull + 2;     // leader: accumulator set drained (kSlots)
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   __shared__ int abort_flag;
@@ -84,9 +87,9 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
       mbar_init(&conv[s], Cfg::kTransformThreads * PAIR);
       mbar_init(&rawfull[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kSlots; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128 * PAIR);
+      mbar_init(&tempty[b], Cfg::kEpiThreads * PAIR);
     }
     mbar_init(drain, 1);
     abort_flag = 0;
@@ -134,6 +137,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
         const uint32_t n_mma = mma_n(tile.valid & 0xFFFF, BN);
         const int a_row = tile.w_row + (int)rank * 128;
+        const int n_a = FA == 2 && (tile.valid >> 16) > 128 ? 2 : 1;  // weight tiles loaded
         const int b_row = tile.x_row + (int)rank * (int)(n_mma / PAIR);
         int x_map = 0;  // single CTAs: the smallest token box covering n_mma rows
         while (PAIR == 1 && (uint32_t)token_box_rows(x_map) < n_mma) ++x_map;
@@ -150,16 +154,17 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
           // quantized raw weight tiles complete on this CTA's `rawfull`.
           if (leader)
             mbar_arrive_expect_tx(&full[stage],
-                                  PAIR * ((kQuant ? 0 : Cfg::kABytes) +
+                                  PAIR * ((kQuant ? 0 : Cfg::kATileBytes * n_a) +
                                           (PAIR == 2 ? Cfg::kBBytes : x_box * 128)));
           if (kQuant) {
-            mbar_arrive_expect_tx(&rawfull[stage], Cfg::kRawBytes);
-            if (WK == WK_INT8)
-              tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &rawfull[stage], wkb * 64,
-                          a_row);
-            else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
-              tma_load_2d(raw_tiles + stage * Cfg::kRawBytes, &wmap, &rawfull[stage],
-                          a_row >> 1, wkb * 64);
+            mbar_arrive_expect_tx(&rawfull[stage], Cfg::kRawTileBytes * n_a);
+            for (int ai = 0; ai < n_a; ++ai) {
+              uint8_t *dst = raw_tiles + stage * Cfg::kRawBytes + ai * Cfg::kRawTileBytes;
+              if (WK == WK_INT8)
+                tma_load_2d(dst, &wmap, &rawfull[stage], wkb * 64, a_row + ai * 128);
+              else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
+                tma_load_2d(dst, &wmap, &rawfull[stage], (a_row + ai * 128) >> 1, wkb * 64);
+            }
           }
           if (PAIR == 2) {
             const uint32_t fb = leader_bar(&full[stage]);
@@ -168,7 +173,9 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
             tma_load_2d_pair(b_tiles + stage * Cfg::kBBytes, &xmaps.m[0], fb, xkb * 64, b_row);
           } else {
             if (!kQuant)
-              tma_load_2d(a_tiles + stage * Cfg::kABytes, &wmap, &full[stage], wkb * 64, a_row);
+              for (int ai = 0; ai < n_a; ++ai)
+                tma_load_2d(a_tiles + stage * Cfg::kABytes + ai * Cfg::kATileBytes, &wmap,
+                            &full[stage], wkb * 64, a_row + ai * 128);
             tma_load_2d(b_tiles + stage * Cfg::kBBytes, &xmaps.m[x_map], &full[stage], xkb * 64,
                         b_row);
           }
@@ -202,13 +209,14 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         TcTile tile;
         int k_begin, k_count, split;
         load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
-        const uint32_t idesc = idesc_bf16_f32(FH, mma_n(tile.valid & 0xFFFF, BN));
+        const uint32_t idesc = idesc_bf16_f32(128 * PAIR, mma_n(tile.valid & 0xFFFF, BN));
+        const int n_a = FA == 2 && (tile.valid >> 16) > 128 ? 2 : 1;
         if (*abort_v || !mbar_wait(&tempty[acc], acc_phase ^ 1, err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * FA * BN);
         for (int kb = 0; kb < k_count; ++kb) {
           bool got = mbar_wait(&full[stage], phase, err);
           if (kQuant && got) got = mbar_wait(&conv[stage], phase, err);
@@ -218,14 +226,17 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
           }
           // (the mbarrier wait orders the TMA-written operands for the MMA; no
           // tcgen05 fence is needed per stage)
-          const uint64_t ad = smem_desc_sw128(a_base + stage * Cfg::kABytes);
           const uint64_t bd = smem_desc_sw128(b_base + stage * Cfg::kBBytes);
+          for (int ai = 0; ai < n_a; ++ai) {
+            const uint64_t ad =
+                smem_desc_sw128(a_base + stage * Cfg::kABytes + ai * Cfg::kATileBytes);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // 4 x K=16 steps, +32 bytes each (encoded >>4: +2)
-            if (PAIR == 2)
-              tc_mma_bf16_pair(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
-            else
-              tc_mma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+            for (int j = 0; j < 4; ++j) {  // 4 x K=16 steps, +32 bytes each (encoded >>4: +2)
+              if (PAIR == 2)
+                tc_mma_bf16_pair(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+              else
+                tc_mma_bf16(d_tmem + ai * BN, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+            }
           }
           if (PAIR == 2) {
             tc_commit_pair(mapa_cta(smem_u32(&empty[stage]), 0));
@@ -245,7 +256,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         } else {
           tc_commit(&tfull[acc]);
         }
-        if (++acc == 2) {
+        if (++acc == kSlots) {
           acc = 0;
           acc_phase ^= 1;
         }
@@ -262,10 +273,11 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
     } else if (lane == 0 && PAIR == 2) {
       mbar_wait(drain, 0, err);  // peer: the leader's last MMAs wrote our TMEM too
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
-    const int i = quarter * 32 + lane;  // feature row within this CTA's 128
+    const int sub = (warp - 2) >> 2;    // accumulator of this warp (FA == 2)
+    const int i = sub * 128 + quarter * 32 + lane;  // feature row within this CTA's tile
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = cluster_id; t < num_tiles; t += clusters) {
@@ -289,42 +301,87 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
         if (args.row_scale) mul *= args.row_scale[f];
         if (args.bias) add = args.bias[f];
       }
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      const int chunks = (t_valid + 15) >> 4;
-      for (int c = 0; c < chunks; ++c) {
-        float v[16];
-        tmem_ld16(taddr + c * 16, v);
-        if (frow) {
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                             (uint32_t)((acc * FA + sub) * BN);
+      // (FA == 2: a tile of <= 128 features leaves the second accumulator unused)
+      const int chunks = sub * 128 < f_valid ? (t_valid + 15) >> 4 : 0;
+      if (FA == 2 && !args.y_f32 && !args.tok_scale) {
+        // One accumulator set: read it all into registers (bf16 pairs), hand
+        // TMEM back to the MMA warp, then store while the next tile runs.
+        uint32_t pk[BN / 2];
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = c * 16 + jj;
-            if (j < t_valid) {
-              float o = v[jj] * mul + add;
-              if (args.relu2) o = nk_relu2(o);
-              if (args.tok_scale) o *= args.tok_scale[tile.x_row + j];
-              const long long off = (long long)(tile.x_row + j) * args.ldy + tile.out_col0 + fi +
-                                    split * args.split_stride;
-              if (args.y_f32)
-                reinterpret_cast<float *>(args.y)[off] = o;
-              else
-                reinterpret_cast<__nv_bfloat16 *>(args.y)[off] = __float2bfloat16_rn(o);
+        for (int c = 0; c < BN / 16; ++c) {
+          if (c < chunks) {
+            float v[16];
+            tmem_ld16(taddr + c * 16, v);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float o0 = v[2 * q] * mul + add, o1 = v[2 * q + 1] * mul + add;
+              if (args.relu2) {
+                o0 = nk_relu2(o0);
+                o1 = nk_relu2(o1);
+              }
+              __nv_bfloat162 b = __floats2bfloat162_rn(o0, o1);
+              pk[c * 8 + q] = *reinterpret_cast<uint32_t *>(&b);
             }
           }
         }
-      }
-      tc_fence_before();
-      if (PAIR == 2)
-        mbar_arrive_cluster(leader_bar(&tempty[acc]));
-      else
+        tc_fence_before();
         mbar_arrive(&tempty[acc]);
-      if (++acc == 2) {
+        if (frow) {
+          __nv_bfloat16 *yb = reinterpret_cast<__nv_bfloat16 *>(args.y) + tile.out_col0 + fi +
+                              (long long)split * args.split_stride;
+#pragma unroll
+          for (int c = 0; c < BN / 16; ++c) {
+            if (c < chunks) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const int j = c * 16 + jj;
+                if (j < t_valid) {
+                  const uint32_t w = pk[c * 8 + (jj >> 1)];
+                  const unsigned short h = (jj & 1) ? (unsigned short)(w >> 16) : (unsigned short)w;
+                  reinterpret_cast<unsigned short *>(yb)[(long long)(tile.x_row + j) * args.ldy] = h;
+                }
+              }
+            }
+          }
+        }
+      } else {
+        for (int c = 0; c < chunks; ++c) {
+          float v[16];
+          tmem_ld16(taddr + c * 16, v);
+          if (frow) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = c * 16 + jj;
+              if (j < t_valid) {
+                float o = v[jj] * mul + add;
+                if (args.relu2) o = nk_relu2(o);
+                if (args.tok_scale) o *= args.tok_scale[tile.x_row + j];
+                const long long off = (long long)(tile.x_row + j) * args.ldy + tile.out_col0 +
+                                      fi + split * args.split_stride;
+                if (args.y_f32)
+                  reinterpret_cast<float *>(args.y)[off] = o;
+                else
+                  reinterpret_cast<__nv_bfloat16 *>(args.y)[off] = __float2bfloat16_rn(o);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        if (PAIR == 2)
+          mbar_arrive_cluster(leader_bar(&tempty[acc]));
+        else
+          mbar_arrive(&tempty[acc]);
+      }
+      if (++acc == kSlots) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
   } else if (kQuant) {
     // ------------------------------------------------------------ transform
-    const int tid = threadIdx.x - 192;  // 0 .. kTransformThreads-1
+    const int tid = threadIdx.x - 64 - Cfg::kEpiThreads;  // 0 .. kTransformThreads-1
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -338,12 +395,15 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR>::kThreads, 1)
           ok = false;
           break;
         }
-        const uint8_t *raw = raw_tiles + stage * Cfg::kRawBytes;
-        uint8_t *dst = a_tiles + stage * Cfg::kABytes;
         constexpr int kTT = Cfg::kTransformThreads > 0 ? Cfg::kTransformThreads : 1;
+        const int n_a = FA == 2 && (tile.valid >> 16) > 128 ? 2 : 1;
 #pragma unroll
-        for (int q = 0; q < 1024 / kTT; ++q) {
-          const int idx = q * kTT + tid;
+        for (int q = 0; q < 1024 * FA / kTT; ++q) {
+          const int ai = (q * kTT + tid) >> 10;
+          if (ai >= n_a) continue;
+          const int idx = (q * kTT + tid) & 1023;
+          const uint8_t *raw = raw_tiles + stage * Cfg::kRawBytes + ai * Cfg::kRawTileBytes;
+          uint8_t *dst = a_tiles + stage * Cfg::kABytes + ai * Cfg::kATileBytes;
           int row, c;
           uint32_t packed[4];
           if (WK == WK_INT8) {
@@ -496,17 +556,22 @@ nk_status make_map(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes, con
   return NK_OK;
 }
 
-template <int WK, int BN, int PAIR>
+// The dynamic shared memory limit is a per-device property of the function:
+// set once per (instantiation, device).
+template <int WK, int BN, int PAIR, int FA>
 nk_status launch_impl(const CUtensorMap &wm, const TokenMaps &xm, const TcArgs &args, int grid,
                       cudaStream_t stream) {
-  using Cfg = TcConfig<WK, BN, PAIR>;
-  static bool attr_done = false;  // benign race: setting the attribute twice is harmless
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WK, BN, PAIR>,
+  using Cfg = TcConfig<WK, BN, PAIR, FA>;
+  static std::atomic<bool> attr_done[64];
+  int dev = 0;
+  NK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(NK_DEVICE_ERROR, "device ordinal out of range");
+  if (!attr_done[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WK, BN, PAIR, FA>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmemBytes);
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(tc_gemm)");
-    attr_done = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
@@ -522,17 +587,18 @@ nk_status launch_impl(const CUtensorMap &wm, const TokenMaps &xm, const TcArgs &
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = PAIR == 2 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WK, BN, PAIR>, wm, xm, args);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WK, BN, PAIR, FA>, wm, xm, args);
   if (e != cudaSuccess) return fail_cuda(e, "cudaLaunchKernelEx(tc_gemm)");
   return check_launch("tc_gemm_kernel pair");
 }
 
 template <int WK>
-nk_status launch_kind(int bn, int pair, const CUtensorMap &wm, const TokenMaps &xm,
+nk_status launch_kind(int bn, int pair, int fa, const CUtensorMap &wm, const TokenMaps &xm,
                       const TcArgs &args, int grid, cudaStream_t stream) {
-  if (pair == 2) return launch_impl<WK, 256, 2>(wm, xm, args, grid, stream);
-  return bn == 256 ? launch_impl<WK, 256, 1>(wm, xm, args, grid, stream)
-                   : launch_impl<WK, 64, 1>(wm, xm, args, grid, stream);
+  if (pair == 2) return launch_impl<WK, 256, 2, 1>(wm, xm, args, grid, stream);
+  if (fa == 2) return launch_impl<WK, 256, 1, 2>(wm, xm, args, grid, stream);
+  return bn == 256 ? launch_impl<WK, 256, 1, 1>(wm, xm, args, grid, stream)
+                   : launch_impl<WK, 64, 1, 1>(wm, xm, args, grid, stream);
 }
 
 }  // namespace
@@ -540,9 +606,11 @@ nk_status launch_kind(int bn, int pair, const CUtensorMap &wm, const TokenMaps &
 // See gemm_tc.h.  w: bf16 [n_w_rows, ldw] / int8 [n_w_rows, ldw] / int4 bytes [K, N/2].
 nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ldw_bytes,
                   const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
-                  TcArgs args, int grid, cudaStream_t stream, int pair) {
+                  TcArgs args, int grid, cudaStream_t stream, int pair, int fa) {
   if (pair == 2 && (bn != 256 || (grid & 1)))
     return fail(NK_UNSUPPORTED, "CTA pairs need 256-token tiles and an even grid");
+  if (fa == 2 && (bn != 256 || pair != 1))
+    return fail(NK_UNSUPPORTED, "two accumulators need 256-token tiles on single CTAs");
   CUtensorMap wm;
   nk_status st;
   if (wk == WK_BF16)
@@ -568,9 +636,9 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
     if (st != NK_OK) return st;
   }
   if (grid <= 0) return ok();
-  if (wk == WK_BF16) return launch_kind<WK_BF16>(bn, pair, wm, xm, args, grid, stream);
-  if (wk == WK_INT8) return launch_kind<WK_INT8>(bn, pair, wm, xm, args, grid, stream);
-  return launch_kind<WK_INT4KN>(bn, pair, wm, xm, args, grid, stream);
+  if (wk == WK_BF16) return launch_kind<WK_BF16>(bn, pair, fa, wm, xm, args, grid, stream);
+  if (wk == WK_INT8) return launch_kind<WK_INT8>(bn, pair, fa, wm, xm, args, grid, stream);
+  return launch_kind<WK_INT4KN>(bn, pair, fa, wm, xm, args, grid, stream);
 }
 
 }  // namespace nk

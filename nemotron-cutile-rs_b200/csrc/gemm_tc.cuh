@@ -77,15 +77,22 @@ struct WeightTile {
   static constexpr int kRawBytes = WK == WK_BF16 ? 0 : (WK == WK_INT8 ? 128 * 64 : 64 * 64);
 };
 
-// PAIR = 1: one CTA computes 128 features x BN tokens.
+// PAIR = 1: one CTA computes 128·FA features x BN tokens.
 // PAIR = 2: a cluster of two CTAs computes 256 features x BN tokens with
 // tcgen05.mma.cta_group::2; each CTA holds 128 weight rows and BN/2 token rows.
-template <int WK, int BN, int PAIR = 1>
+// FA = 2 (single CTAs, bf16 weights): each stage carries two 128-row weight
+// tiles against one token tile, accumulated in two TMEM accumulators (2·BN
+// columns: the whole tile set, so there is one accumulator set instead of two
+// double-buffered ones); the token bytes per weight byte halve.
+template <int WK, int BN, int PAIR = 1, int FA = 1>
 struct TcConfig {
-  static constexpr int kABytes = 128 * 128;         // 128 weight rows x 64 bf16
+  static_assert(FA == 1 || (FA == 2 && PAIR == 1), "two accumulators only for single CTAs");
+  static constexpr int kATileBytes = 128 * 128;     // 128 weight rows x 64 bf16
+  static constexpr int kABytes = kATileBytes * FA;
   static constexpr int kBRows = BN / PAIR;          // token rows loaded per CTA
   static constexpr int kBBytes = kBRows * 128;      // kBRows x 64 bf16
-  static constexpr int kRawBytes = WeightTile<WK>::kRawBytes;
+  static constexpr int kRawTileBytes = WeightTile<WK>::kRawBytes;
+  static constexpr int kRawBytes = kRawTileBytes * FA;
   static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
   static constexpr int kStages0 = (224 * 1024) / kStageBytes;
 #ifndef NK_STAGES_MAX
@@ -95,11 +102,13 @@ struct TcConfig {
 #ifndef NK_TRANSFORM_THREADS
 #define NK_TRANSFORM_THREADS 256
 #endif
-  static constexpr int kTransformThreads = WK == WK_BF16 ? 0 : NK_TRANSFORM_THREADS;
-  static constexpr int kThreads = 192 + kTransformThreads;
+  static constexpr int kTransformThreads = WK == WK_BF16 ? 0 : NK_TRANSFORM_THREADS * FA;
+  static constexpr int kEpiThreads = 128 * FA;      // 4 warps per accumulator
+  static constexpr int kThreads = 64 + kEpiThreads + kTransformThreads;
+  static constexpr int kAccSlots = 2 / FA;          // accumulator sets in TMEM
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
-  static constexpr int kFeatRows = 128 * PAIR;      // features per output tile
+  static constexpr int kFeatRows = 128 * PAIR * FA; // features per output tile
 };
 
 }  // namespace nk

@@ -12,8 +12,10 @@ namespace nk {
 // pair = 2: clusters of two CTAs share 256-feature tiles (tcgen05 cta_group::2);
 // needs bn = 256, an even grid, and tiles of 256 features (f_tiles / tile lists
 // built with 256-row feature tiles).
+// fa = 2: single CTAs with two accumulators: 256-feature tiles (lists built
+// with 256-row feature tiles), bn = 256.
 nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ldw_bytes,
                   const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
-                  TcArgs args, int grid, cudaStream_t stream, int pair = 1);
+                  TcArgs args, int grid, cudaStream_t stream, int pair = 1, int fa = 1);
 
 }  // namespace nk

@@ -16,7 +16,7 @@ constexpr int kRouterMaxSplits = 16;
 
 // Grouped tile lists over row segments: segment s holds seg_rows[s]
 // contiguous rows (segments back to back) for expert seg_expert[s] (identity
-// when null).  Each segment gets ceil(n_out/128) feature tiles x
+// when null).  Each segment gets ceil(n_out/fh) feature tiles of fh rows x
 // ceil(rows/BN) token tiles, feature-major within the segment.  Block b
 // builds list b (n_out[b], tiles[b], count[b]): the up and the down
 // projection in one launch.  n_seg <= 1024; after a scan of the per-segment
@@ -29,13 +29,14 @@ struct TileLists {
 
 __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__restrict__ seg_rows,
                                                            const int32_t *__restrict__ seg_expert,
-                                                           int n_seg, int bn, TileLists lists) {
+                                                           int n_seg, int bn, int fh,
+                                                           TileLists lists) {
   __shared__ int tiles_sc[1024];
   __shared__ int rows_sc[1024];
   const int s = threadIdx.x;
   const int n_out = lists.n_out[blockIdx.x];
   TcTile *tiles = lists.tiles[blockIdx.x];
-  const int ft = (n_out + 127) / 128;
+  const int ft = (n_out + fh - 1) / fh;
   const int c = s < n_seg ? seg_rows[s] : 0;
   const int mine = ft * ((c + bn - 1) / bn);
   tiles_sc[s] = mine;
@@ -65,11 +66,11 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
     const int f = local / tt, t = local - f * tt;
     const int e = seg_expert ? seg_expert[seg] : seg;
     TcTile tile;
-    tile.w_row = e * n_out + f * 128;
+    tile.w_row = e * n_out + f * fh;
     tile.x_row = rows_sc[seg] - rows + t * bn;
-    const int fv = n_out - f * 128, tv = rows - t * bn;
-    tile.valid = ((fv > 128 ? 128 : fv) << 16) | (tv > bn ? bn : tv);
-    tile.out_col0 = f * 128;
+    const int fv = n_out - f * fh, tv = rows - t * bn;
+    tile.valid = ((fv > fh ? fh : fv) << 16) | (tv > bn ? bn : tv);
+    tile.out_col0 = f * fh;
     tiles[j] = tile;
   }
 }
@@ -311,6 +312,16 @@ TcArgs base_args(int *err) {
 }
 
 // Dense Y[T, n_out] = act(X[T, k] · W[n_out, k]ᵀ ...) through the tcgen05 kernel.
+// Accumulators per CTA for the grouped bf16 expert GEMMs (NK_GROUPED_FA=1
+// selects the one-accumulator kernel, for comparison).
+int grouped_fa() {
+  static const int v = [] {
+    const char *e = getenv("NK_GROUPED_FA");
+    return e && atoi(e) == 1 ? 1 : 2;
+  }();
+  return v;
+}
+
 nk_status dense(int wk, const void *w, const float *row_scale, const float *bias,
                 const uint16_t *x, int64_t T, int64_t k, int64_t n_out, void *y, bool y_f32,
                 bool relu2, int *err, cudaStream_t s, int max_ctas = 0) {
@@ -408,6 +419,9 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   int *err = device_error_ptr();
   const int64_t E = L.experts, H = L.hidden, I = L.inter;
   const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
+  // bf16 experts: 256-feature tiles with two accumulators per CTA (each
+  // token tile is loaded once per 256 features instead of once per 128)
+  const int fa = wk == WK_BF16 ? grouped_fa() : 1;
   TileLists lists;
   lists.n_out[0] = (int)I;
   lists.n_out[1] = (int)H;
@@ -415,7 +429,7 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   lists.tiles[1] = ws.tiles_down;
   lists.count[0] = ws.tile_counts;
   lists.count[1] = ws.tile_counts + 1;
-  build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, lists);
+  build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, 128 * fa, lists);
   nk_status st = check_launch("build_tiles_kernel");
   if (st != NK_OK) return st;
   if (R == 0) return NK_OK;
@@ -431,7 +445,7 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
     a.bias = L.up_b;
     a.relu2 = 1;
     st = tc_gemm(wk, L.up_w, E * I, H, wk == WK_BF16 ? 2 * H : H, rows, R, H, H, kMoeBN, a,
-                 ctas, s);
+                 ctas, s, 1, fa);
     if (st != NK_OK) return st;
   }
   tm.mark(4, s);
@@ -445,7 +459,7 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
     a.row_scale = wk == WK_INT8 ? L.down_scale : nullptr;
     a.bias = L.down_b;
     st = tc_gemm(wk, L.down_w, E * H, I, wk == WK_BF16 ? 2 * I : I, ws.hmid, R, I, I, kMoeBN, a,
-                 ctas, s);
+                 ctas, s, 1, fa);
   }
   return st;
 }
