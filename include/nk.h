@@ -108,11 +108,21 @@ nk_status nk_gemm_f32(const float *lhs, size_t lhs_len, const float *rhs, size_t
  * (mamba2.rs:229-263,353-359), attention Q/K/V/O (attention.rs:170-209) and the
  * MLP/MoE experts (mlp.rs:201-208) call:
  *   Y[M,N] = epilogue( X[M,K] · Wᵀ ),  W stored [N,K] (K contiguous).
- * x_dtype: NK_BF16 or NK_F32 (f32 activations are split exactly into two
- * bf16 halves, so the product keeps ~16 mantissa bits).  y_dtype: NK_BF16 or
- * NK_F32.  bias: f32 [N] or NULL, added after the GEMM as linear.rs:333-339
- * does.  flags: NK_EPI_RELU2 applies relu2 (activations.rs:68-71) after the
- * bias, fusing mlp.rs:205.  Accumulation is f32 in tensor memory. */
+ * x_dtype: NK_BF16 or NK_F32 (f32 activations are split into two bf16
+ * halves, hi + lo, which keep the top 16 of the 24 significand bits, so the
+ * product carries ~16 mantissa bits of x).  y_dtype: NK_BF16 or NK_F32.
+ * bias: f32 [N] or NULL, added after the GEMM as linear.rs:333-339 does.
+ * flags: NK_EPI_RELU2 applies relu2 (activations.rs:68-71) after the bias,
+ * fusing mlp.rs:205.  Accumulation is f32 in tensor memory.
+ *
+ * Scratch: decode shapes split K over CTAs (f32 partial sums) and f32
+ * activations need their bf16 split; these calls keep that scratch in a
+ * library block per (device, stream), grown on first need (cudaMalloc) and
+ * reused.  Calls on different streams never share it; calls on one stream
+ * are ordered by the stream.  Growth is refused with NK_WORKSPACE_TOO_SMALL
+ * while the stream is being captured into a CUDA graph: run each shape once
+ * before capturing.  nk_scratch_release frees a stream's block.  The *_ws
+ * forms below take caller-owned scratch instead and allocate nothing. */
 nk_status nk_gemm_bf16(const void *x, int32_t x_dtype, const uint16_t *w, const float *bias,
                        void *y, int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
                        void *stream);
@@ -140,11 +150,37 @@ nk_status nk_gemm_w4a(const void *x, int32_t x_dtype, const uint8_t *packed, siz
                       int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
                       void *stream);
 
+/* Scratch bytes a projection of this shape needs (0 when none):
+ * weight_kind NK_W_BF16 / NK_W_INT8_ROW / NK_W_INT4_AFFINE, x_dtype as above.
+ * The same shapes and kinds always need the same bytes on one device. */
+nk_status nk_gemm_workspace_bytes(int32_t weight_kind, int32_t x_dtype, int64_t m, int64_t k,
+                                  int64_t n, size_t *bytes);
+
+/* nk_gemm_bf16 / nk_gemm_w8row / nk_gemm_w4a with caller-owned scratch
+ * (device memory of at least nk_gemm_workspace_bytes; may be NULL when that
+ * is 0): re-entrant across host threads and streams as long as concurrent
+ * calls get distinct workspaces.  NK_WORKSPACE_TOO_SMALL when it is short. */
+nk_status nk_gemm_bf16_ws(const void *x, int32_t x_dtype, const uint16_t *w, const float *bias,
+                          void *y, int32_t y_dtype, int64_t m, int64_t k, int64_t n,
+                          int32_t flags, void *workspace, size_t workspace_bytes, void *stream);
+nk_status nk_gemm_w8row_ws(const void *x, int32_t x_dtype, const int8_t *wq, const float *scales,
+                           const float *bias, void *y, int32_t y_dtype, int64_t m, int64_t k,
+                           int64_t n, int32_t flags, void *workspace, size_t workspace_bytes,
+                           void *stream);
+nk_status nk_gemm_w4a_ws(const void *x, int32_t x_dtype, const uint8_t *packed, size_t packed_len,
+                         float scale, uint32_t zero_point, const float *bias, void *y,
+                         int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
+/* Frees the library scratch block of `stream` on the current device (after
+ * the stream's queued work).  The next call on that stream allocates again. */
+nk_status nk_scratch_release(void *stream);
+
 /* Allocation-free variant of nk_gemm_w8row for f32 activations.  It has no
  * counterpart in the reference.  For callers that cannot let a library call
  * cudaMalloc (a host whose device memory belongs to its own pool, or a
  * latency-critical path where an allocation would synchronise the device):
- * the exact bf16 split of x lives in a fixed 8 MiB device array inside
+ * the bf16 hi | lo split of x lives in a fixed 8 MiB device array inside
  * libnk, held by every GPU that loads the library until exit, instead of the
  * library's growable scratch.  m * 4 * ceil(k/64)*64 bytes must fit in 8 MiB
  * (NK_WORKSPACE_TOO_SMALL otherwise); k % 16 == 0.  All calls on a device
@@ -223,7 +259,7 @@ nk_status nk_moe_plan(const int32_t *indices, int64_t tokens, int64_t top_k, int
 
 /* -------------------------------------------------------------- MoE layer */
 
-enum { NK_W_BF16 = 0, NK_W_INT8_ROW = 1 };
+enum { NK_W_BF16 = 0, NK_W_INT8_ROW = 1, NK_W_INT4_AFFINE = 2 };
 
 /* Weights of one MoE layer, all device pointers, in the layouts the B200
  * kernels read (each GEMM weight is [out_features, in_features], K contiguous;

@@ -1,6 +1,8 @@
 // common.cu — thread-local error record, per-device error word and scratch
 // arena, and the library-level entry points of nk.h.
+#include <map>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "nk_common.cuh"
@@ -33,9 +35,15 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 int *g_err_ptr[kMaxDevices];
-void *g_scratch[kMaxDevices];
-size_t g_scratch_bytes[kMaxDevices];
 int g_sms[kMaxDevices];
+
+// Library scratch: one block per (device, stream), so calls on different
+// streams never share split-K partials or staging buffers.
+struct Arena {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, Arena> g_arenas;
 
 int current_device() {
   int d = 0;
@@ -67,24 +75,50 @@ int num_sms() {
   return g_sms[d];
 }
 
-// The arena only grows.  Growth synchronises the device first so that no
-// queued kernel still uses the old block.
-nk_status scratch(size_t bytes, void **ptr, cudaStream_t) {
+// The stream's block only grows.  Growth waits for the stream (only its own
+// work uses the block) and is refused while the stream is being captured: a
+// captured graph would keep the address of a block freed later.  Warm up at
+// the largest shape before capturing.
+nk_status scratch(size_t bytes, void **ptr, cudaStream_t stream) {
   int d = current_device();
   if (d < 0 || d >= kMaxDevices) return fail(NK_DEVICE_ERROR, "device ordinal out of range");
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_scratch_bytes[d] < bytes) {
-    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
-    if (g_scratch[d]) {
-      NK_CUDA_TRY(cudaDeviceSynchronize());
-      NK_CUDA_TRY(cudaFree(g_scratch[d]));
-      g_scratch[d] = nullptr;
-      g_scratch_bytes[d] = 0;
+  Arena &a = g_arenas[std::make_pair(d, stream)];
+  if (a.bytes < bytes) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    NK_CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
+    if (cs != cudaStreamCaptureStatusNone) {
+      nk_status st = fail(NK_WORKSPACE_TOO_SMALL,
+                          "library scratch must grow, which is not allowed during stream capture: "
+                          "run the call once at its largest shape before capturing");
+      tls_error().expected = bytes;
+      tls_error().actual = a.bytes;
+      return st;
     }
-    NK_CUDA_TRY(cudaMalloc(&g_scratch[d], want));
-    g_scratch_bytes[d] = want;
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    if (a.ptr) {
+      NK_CUDA_TRY(cudaStreamSynchronize(stream));
+      NK_CUDA_TRY(cudaFree(a.ptr));
+      a.ptr = nullptr;
+      a.bytes = 0;
+    }
+    NK_CUDA_TRY(cudaMalloc(&a.ptr, want));
+    a.bytes = want;
   }
-  *ptr = g_scratch[d];
+  *ptr = a.ptr;
+  return NK_OK;
+}
+
+nk_status release_scratch(cudaStream_t stream) {
+  int d = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_arenas.find(std::make_pair(d, stream));
+  if (it == g_arenas.end()) return NK_OK;
+  if (it->second.ptr) {
+    NK_CUDA_TRY(cudaStreamSynchronize(stream));
+    NK_CUDA_TRY(cudaFree(it->second.ptr));
+  }
+  g_arenas.erase(it);
   return NK_OK;
 }
 
@@ -98,6 +132,11 @@ nk_status nk_last_error(nk_error_info *out) {
 }
 
 int32_t nk_version(void) { return 100; }
+
+nk_status nk_scratch_release(void *stream) {
+  nk_status st = nk::release_scratch(nk::as_stream(stream));
+  return st == NK_OK ? nk::ok() : st;
+}
 
 nk_status nk_selftest_wait_timeout(void *stream) {
   int *err = nk::device_error_ptr();

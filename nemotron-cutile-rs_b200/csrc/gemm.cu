@@ -55,8 +55,10 @@ __global__ void __launch_bounds__(256) gemm_f32_f64acc_kernel(const float *__res
 }
 
 // ------------------------------------------------------- projection helpers
-// Exact two-way split of f32 activations into bf16 hi | lo halves, written
-// as X2[m, 0:Kp] = hi, X2[m, Kp:2Kp] = lo (zero padded to Kp = ceil(K/64)*64).
+// Two-way split of f32 activations into bf16 hi | lo halves, written as
+// X2[m, 0:Kp] = hi, X2[m, Kp:2Kp] = lo (zero padded to Kp = ceil(K/64)*64).
+// hi + lo keeps the top 16 of the 24 significand bits (relative error below
+// 2^-16 per element), well inside the f32-activation bar of 1e-3.
 __global__ void split_f32_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ x2,
                                  int64_t M, int64_t K, int64_t Kp) {
   int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -67,6 +69,14 @@ __global__ void split_f32_kernel(const float *__restrict__ x, __nv_bfloat16 *__r
   __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
   x2[m * 2 * Kp + k] = hi;
   x2[m * 2 * Kp + Kp + k] = lo;
+}
+
+nk_status launch_split_f32(const float *x, int64_t m, int64_t k, int64_t kp, uint16_t *x2,
+                           cudaStream_t stream) {
+  const int64_t total = m * kp;
+  split_f32_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, stream>>>(
+      x, reinterpret_cast<__nv_bfloat16 *>(x2), m, k, kp);
+  return check_launch("split_f32_kernel");
 }
 
 // Plain CUDA projection for shapes outside the TMA envelope: one thread per
@@ -186,25 +196,121 @@ static int choose_k_splits(int f_tiles, int t_tiles, int k_blocks, int sms, doub
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Shared driver for nk_gemm_bf16 / nk_gemm_w8row / nk_gemm_w4a.
-nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_scale, int zp,
-                     const float *row_scale, const float *bias, void *y, int y_dtype,
-                     int64_t m, int64_t k, int64_t n, int flags, cudaStream_t stream) {
+// How one projection runs: which kernel, its K splits and the scratch it
+// needs ([split activations (f32 x)] [split-K partial sums]).
+struct ProjPlan {
+  enum { SIMT, GEMV, TC } path;
+  int gemv_splits = 1;
+  int64_t gemv_kps = 0;
+  int k_blocks = 0, w_period = 0, bn = 0, splits = 1, pair = 1;
+  int64_t kp = 0;
+  size_t xsplit_bytes = 0, part_off = 0, part_bytes = 0, scratch_bytes = 0;
+};
+
+static ProjPlan plan_projection(int wk, bool aligned, int x_dtype, int64_t m, int64_t k,
+                                int64_t n) {
+  ProjPlan p;
+  bool tc_ok = aligned;
+  if (wk == WK_BF16) tc_ok &= (k % 8) == 0;
+  if (wk == WK_INT8) tc_ok &= (k % 16) == 0;
+  if (wk == WK_INT4KN) tc_ok &= (n % 32) == 0;
+  if (x_dtype == NK_BF16) tc_ok &= (k % 8) == 0;
+  if (!tc_ok) {
+    p.path = ProjPlan::SIMT;
+    return p;
+  }
+  // One or two token rows: stream the weights through registers (gemv.cu);
+  // measured faster than the tensor-core kernel there, slower from 4 rows.
+  // NK_GEMV=0 keeps such shapes on the tensor-core kernel (a tuning probe).
+  static const bool gemv_on = [] {
+    const char *e = getenv("NK_GEMV");
+    return !(e && e[0] == '0');
+  }();
+  if (gemv_on && m <= 2 && (wk == WK_BF16 || wk == WK_INT8) && (k % 16) == 0 &&
+      (x_dtype == NK_BF16 || (k % 4) == 0)) {
+    p.path = ProjPlan::GEMV;
+    p.gemv_splits = gemv_splits(wk, n, k, &p.gemv_kps);
+    p.part_bytes = p.gemv_splits > 1 ? (size_t)p.gemv_splits * m * n * 4 : 0;
+    p.scratch_bytes = p.part_bytes;
+    return p;
+  }
+  p.path = ProjPlan::TC;
+  p.k_blocks = (int)ceil_div(k, 64);
+  p.kp = ceil_div(k, 64) * 64;
+  if (x_dtype == NK_F32) {
+    p.w_period = (int)(p.kp / 64);
+    p.k_blocks = 2 * p.w_period;
+  }
+  p.bn = m <= 64 ? 64 : 256;
+  const int f_tiles = (int)ceil_div(n, 128), t_tiles = (int)ceil_div(m, p.bn);
+  const double w_bytes = (double)n * (double)k * (wk == WK_BF16 ? 2.0 : wk == WK_INT8 ? 1.0 : 0.5);
+  int splits = choose_k_splits(f_tiles, t_tiles, p.k_blocks, num_sms(), w_bytes, m, n);
+  if (const char *e = getenv("NK_SPLITK")) {  // tuning override: forced K split count
+    int v = atoi(e);
+    if (v >= 1 && v <= p.k_blocks) splits = v;
+  }
+  {  // every split gets at least one K block
+    const int per = (p.k_blocks + splits - 1) / splits;
+    splits = (p.k_blocks + per - 1) / per;
+  }
+  p.splits = splits;
+  // Prefill shapes (more than one token tile) can run on CTA pairs: 256-feature
+  // tiles, each SM loading half of every token tile.  Measured no faster than
+  // single CTAs for bf16 weights and slower for int8 on B200, so opt-in
+  // (NK_PAIR=1).
+  static const bool pair_ok = [] {
+    const char *e = getenv("NK_PAIR");
+    return e && e[0] == '1';
+  }();
+  p.pair = (pair_ok && t_tiles >= 2 && p.bn == 256) ? 2 : 1;
+  p.xsplit_bytes = x_dtype == NK_F32 ? (size_t)(m * 2 * p.kp * 2) : 0;
+  p.part_off = (p.xsplit_bytes + 255) & ~size_t(255);
+  p.part_bytes = splits > 1 ? (size_t)splits * m * n * 4 : 0;
+  p.scratch_bytes = p.xsplit_bytes + p.part_bytes > 0 ? p.part_off + p.part_bytes : 0;
+  return p;
+}
+
+static nk_status check_proj_args(int x_dtype, int y_dtype, int64_t m, int64_t k, int64_t n) {
   if (m <= 0 || k <= 0 || n <= 0) return fail(NK_INVALID_SHAPE, "m, k and n must be positive");
   if (x_dtype != NK_BF16 && x_dtype != NK_F32) return fail(NK_UNSUPPORTED, "x_dtype");
   if (y_dtype != NK_BF16 && y_dtype != NK_F32) return fail(NK_UNSUPPORTED, "y_dtype");
   if (m > (1ll << 30) || n > (1ll << 30) || k > (1ll << 30))
     return fail(NK_INVALID_SHAPE, "dimension too large");
+  return NK_OK;
+}
+
+// Shared driver for nk_gemm_bf16 / nk_gemm_w8row / nk_gemm_w4a (and their
+// _ws forms).  workspace: caller-owned scratch of at least the planned bytes,
+// or null for the library's per-(device, stream) scratch.
+nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_scale, int zp,
+                     const float *row_scale, const float *bias, void *y, int y_dtype,
+                     int64_t m, int64_t k, int64_t n, int flags, cudaStream_t stream,
+                     void *workspace = nullptr, size_t workspace_bytes = 0) {
+  nk_status st = check_proj_args(x_dtype, y_dtype, m, k, n);
+  if (st != NK_OK) return st;
   int *err = device_error_ptr();
   const bool relu2 = (flags & NK_EPI_RELU2) != 0;
+  const ProjPlan p = plan_projection(wk, aligned16(x) && aligned16(w), x_dtype, m, k, n);
 
-  bool tc_ok = aligned16(x) && aligned16(w);
-  if (wk == WK_BF16) tc_ok &= (k % 8) == 0;
-  if (wk == WK_INT8) tc_ok &= (k % 16) == 0;
-  if (wk == WK_INT4KN) tc_ok &= (n % 32) == 0;
-  if (x_dtype == NK_BF16) tc_ok &= (k % 8) == 0;
+  uint8_t *buf = nullptr;
+  if (p.scratch_bytes > 0) {
+    if (workspace) {
+      if (workspace_bytes < p.scratch_bytes) {
+        st = fail(NK_WORKSPACE_TOO_SMALL, "workspace smaller than nk_gemm_workspace_bytes");
+        tls_error().expected = p.scratch_bytes;
+        tls_error().actual = workspace_bytes;
+        return st;
+      }
+      buf = reinterpret_cast<uint8_t *>(workspace);
+    } else {
+      void *b = nullptr;
+      st = scratch(p.scratch_bytes, &b, stream);
+      if (st != NK_OK) return st;
+      buf = reinterpret_cast<uint8_t *>(b);
+    }
+  }
 
-  if (!tc_ok) {
+  if (p.path == ProjPlan::SIMT) {
     int64_t total = m * n;
     int threads = 256;
     int64_t blocks = (total + threads - 1) / threads;
@@ -223,28 +329,13 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
     return check_launch("proj_simt_kernel");
   }
 
-  // One or two token rows: stream the weights through registers (gemv.cu);
-  // measured faster than the tensor-core kernel there, slower from 4 rows.
-  // NK_GEMV=0 keeps such shapes on the tensor-core kernel (a tuning probe).
-  static const bool gemv_on = [] {
-    const char *e = getenv("NK_GEMV");
-    return !(e && e[0] == '0');
-  }();
-  if (gemv_on && m <= 2 && (wk == WK_BF16 || wk == WK_INT8) && (k % 16) == 0 &&
-      (x_dtype == NK_BF16 || (k % 4) == 0)) {
-    int64_t kps = 0;
-    const int splits = gemv_splits(wk, n, k, &kps);
-    float *part = nullptr;
-    if (splits > 1) {
-      void *b = nullptr;
-      nk_status st = scratch((size_t)splits * m * n * 4, &b, stream);
-      if (st != NK_OK) return st;
-      part = reinterpret_cast<float *>(b);
-    }
-    launch_gemv(wk, x, x_dtype == NK_F32, (int)m, w, n, k, kps, splits, w_scale, row_scale,
-                splits > 1 ? nullptr : bias, splits > 1 ? 0 : (int)relu2, y, y_dtype == NK_F32,
-                part, stream);
-    nk_status st = check_launch("gemv_kernel");
+  if (p.path == ProjPlan::GEMV) {
+    const int splits = p.gemv_splits;
+    float *part = splits > 1 ? reinterpret_cast<float *>(buf) : nullptr;
+    launch_gemv(wk, x, x_dtype == NK_F32, (int)m, w, n, k, p.gemv_kps, splits, w_scale,
+                row_scale, splits > 1 ? nullptr : bias, splits > 1 ? 0 : (int)relu2, y,
+                y_dtype == NK_F32, part, stream);
+    st = check_launch("gemv_kernel");
     if (st != NK_OK || splits == 1) return st;
     return launch_splitk_reduce(part, splits, m * n, n, bias, relu2, y, y_dtype == NK_F32,
                                 stream);
@@ -252,64 +343,23 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
 
   const uint16_t *xb = reinterpret_cast<const uint16_t *>(x);
   int64_t x_k = k, ldx = k;
-  int k_blocks = (int)ceil_div(k, 64);
-  int w_period = 0;
-  const int64_t kp = ceil_div(k, 64) * 64;
   if (x_dtype == NK_F32) {
-    w_period = (int)(kp / 64);
-    k_blocks = 2 * w_period;
-  }
-  const int bn = m <= 64 ? 64 : 256;
-  const int f_tiles = (int)ceil_div(n, 128), t_tiles = (int)ceil_div(m, bn);
-  const double w_bytes = (double)n * (double)k * (wk == WK_BF16 ? 2.0 : wk == WK_INT8 ? 1.0 : 0.5);
-  int splits = choose_k_splits(f_tiles, t_tiles, k_blocks, num_sms(), w_bytes, m, n);
-  if (const char *e = getenv("NK_SPLITK")) {  // tuning override: forced K split count
-    int v = atoi(e);
-    if (v >= 1 && v <= k_blocks) splits = v;
-  }
-  {  // every split gets at least one K block
-    const int per = (k_blocks + splits - 1) / splits;
-    splits = (k_blocks + per - 1) / per;
-  }
-
-  // scratch: [split activations (f32 x)] [split-K partial sums]
-  const size_t xsplit_bytes = x_dtype == NK_F32 ? (size_t)(m * 2 * kp * 2) : 0;
-  const size_t part_off = (xsplit_bytes + 255) & ~size_t(255);
-  const size_t part_bytes = splits > 1 ? (size_t)splits * m * n * 4 : 0;
-  uint8_t *buf = nullptr;
-  if (xsplit_bytes + part_bytes > 0) {
-    void *b = nullptr;
-    nk_status st = scratch(part_off + part_bytes, &b, stream);
-    if (st != NK_OK) return st;
-    buf = reinterpret_cast<uint8_t *>(b);
-  }
-  if (x_dtype == NK_F32) {
-    int64_t total = m * kp;
-    split_f32_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, stream>>>(
-        reinterpret_cast<const float *>(x), reinterpret_cast<__nv_bfloat16 *>(buf), m, k, kp);
-    nk_status st = check_launch("split_f32_kernel");
+    st = launch_split_f32(reinterpret_cast<const float *>(x), m, k, p.kp,
+                          reinterpret_cast<uint16_t *>(buf), stream);
     if (st != NK_OK) return st;
     xb = reinterpret_cast<const uint16_t *>(buf);
-    x_k = 2 * kp;
-    ldx = 2 * kp;
+    x_k = 2 * p.kp;
+    ldx = 2 * p.kp;
   }
-
-  // Prefill shapes (more than one token tile) can run on CTA pairs: 256-feature
-  // tiles, each SM loading half of every token tile.  Measured no faster than
-  // single CTAs for bf16 weights and slower for int8 on B200, so opt-in
-  // (NK_PAIR=1).
-  static const bool pair_ok = [] {
-    const char *e = getenv("NK_PAIR");
-    return e && e[0] == '1';
-  }();
-  const int pair = (pair_ok && t_tiles >= 2 && bn == 256) ? 2 : 1;
+  const int splits = p.splits, pair = p.pair;
+  const int t_tiles = (int)ceil_div(m, p.bn);
   TcArgs a{};
-  a.f_tiles = pair == 2 ? (int)ceil_div(n, 256) : f_tiles;
+  a.f_tiles = (int)ceil_div(n, 128 * pair);
   a.t_tiles = t_tiles;
   a.n_features = (int)n;
   a.n_tokens = (int)m;
-  a.k_blocks = k_blocks;
-  a.w_k_period = w_period;
+  a.k_blocks = p.k_blocks;
+  a.w_k_period = p.w_period;
   a.x_k_period = 0;
   a.w_scale = w_scale;
   a.row_scale = row_scale;
@@ -319,7 +369,7 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
   if (splits > 1) {  // partial sums (row scale is linear, applied per split)
     a.k_splits = splits;
     a.split_stride = m * n;
-    a.y = buf + part_off;
+    a.y = buf + p.part_off;
     a.y_f32 = 1;
   } else {
     a.y = y;
@@ -331,11 +381,15 @@ nk_status projection(int wk, const void *x, int x_dtype, const void *w, float w_
   const int slots = num_sms() / pair;  // concurrent tiles
   int grid = (int)(tiles < slots ? tiles : slots) * pair;
   int64_t ldw_bytes = wk == WK_BF16 ? k * 2 : (wk == WK_INT8 ? k : n / 2);
-  nk_status st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, bn, a, grid, stream, pair);
+  st = tc_gemm(wk, w, n, k, ldw_bytes, xb, m, x_k, ldx, p.bn, a, grid, stream, pair);
   if (st != NK_OK || splits == 1) return st;
   const int64_t mn = m * n;
-  return launch_splitk_reduce(reinterpret_cast<const float *>(buf + part_off), splits, mn, n,
+  return launch_splitk_reduce(reinterpret_cast<const float *>(buf + p.part_off), splits, mn, n,
                               bias, relu2, y, y_dtype == NK_F32, stream);
+}
+
+size_t projection_scratch_bytes(int wk, int x_dtype, int64_t m, int64_t k, int64_t n) {
+  return plan_projection(wk, true, x_dtype, m, k, n).scratch_bytes;
 }
 
 }  // namespace nk
@@ -372,6 +426,52 @@ nk_status nk_gemm_w8row(const void *x, int32_t x_dtype, const int8_t *wq, const 
                         int64_t n, int32_t flags, void *stream) {
   return projection(WK_INT8, x, x_dtype, wq, 1.0f, 0, scales, bias, y, y_dtype, m, k, n, flags,
                     as_stream(stream));
+}
+
+nk_status nk_gemm_workspace_bytes(int32_t weight_kind, int32_t x_dtype, int64_t m, int64_t k,
+                                  int64_t n, size_t *bytes) {
+  nk_status st = check_proj_args(x_dtype, NK_F32, m, k, n);
+  if (st != NK_OK) return st;
+  int wk;
+  if (weight_kind == NK_W_BF16) wk = WK_BF16;
+  else if (weight_kind == NK_W_INT8_ROW) wk = WK_INT8;
+  else if (weight_kind == NK_W_INT4_AFFINE) wk = WK_INT4KN;
+  else return fail(NK_UNSUPPORTED, "weight_kind");
+  if (!bytes) return fail(NK_INVALID_PARAMS, "bytes is null");
+  *bytes = projection_scratch_bytes(wk, x_dtype, m, k, n);
+  return ok();
+}
+
+nk_status nk_gemm_bf16_ws(const void *x, int32_t x_dtype, const uint16_t *w, const float *bias,
+                          void *y, int32_t y_dtype, int64_t m, int64_t k, int64_t n,
+                          int32_t flags, void *workspace, size_t workspace_bytes, void *stream) {
+  nk_status st = projection(WK_BF16, x, x_dtype, w, 1.0f, 0, nullptr, bias, y, y_dtype, m, k, n,
+                            flags, as_stream(stream), workspace, workspace_bytes);
+  return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_gemm_w8row_ws(const void *x, int32_t x_dtype, const int8_t *wq, const float *scales,
+                           const float *bias, void *y, int32_t y_dtype, int64_t m, int64_t k,
+                           int64_t n, int32_t flags, void *workspace, size_t workspace_bytes,
+                           void *stream) {
+  nk_status st = projection(WK_INT8, x, x_dtype, wq, 1.0f, 0, scales, bias, y, y_dtype, m, k, n,
+                            flags, as_stream(stream), workspace, workspace_bytes);
+  return st == NK_OK ? ok() : st;
+}
+
+nk_status nk_gemm_w4a_ws(const void *x, int32_t x_dtype, const uint8_t *packed, size_t packed_len,
+                         float scale, uint32_t zero_point, const float *bias, void *y,
+                         int32_t y_dtype, int64_t m, int64_t k, int64_t n, int32_t flags,
+                         void *workspace, size_t workspace_bytes, void *stream) {
+  if (m <= 0 || k <= 0 || n <= 0) return fail(NK_INVALID_SHAPE, "m, k and n must be positive");
+  nk_status st = nk_validate_int4_params(scale, zero_point);
+  if (st != NK_OK) return st;
+  uint64_t count = (uint64_t)k * (uint64_t)n;
+  uint64_t expect = count / 2 + (count & 1);
+  if (packed_len != expect) return fail_length("packed_weights", expect, packed_len);
+  st = projection(WK_INT4KN, x, x_dtype, packed, scale, (int)zero_point, nullptr, bias, y,
+                  y_dtype, m, k, n, flags, as_stream(stream), workspace, workspace_bytes);
+  return st == NK_OK ? ok() : st;
 }
 
 nk_status nk_gemm_w4a(const void *x, int32_t x_dtype, const uint8_t *packed, size_t packed_len,

@@ -2,7 +2,7 @@
 // activations for callers that must not allocate device memory.
 //
 // The regular entry point (nk_gemm_w8row with x_dtype NK_F32) splits the f32
-// activations into two exact bf16 halves in a library-grown scratch buffer,
+// activations into bf16 hi | lo halves in a library-grown scratch buffer,
 // which may call cudaMalloc.  Some hosts cannot let a library do that: a
 // server or engine that owns all device memory through its own pool and
 // forbids other allocations, or code on a latency-critical path where a
@@ -55,20 +55,6 @@ nk_status static_split_buffer(void **out) {
   return NK_OK;
 }
 
-// x [M,K] f32 -> X2 [M, 2Kp] bf16: hi in columns [0,Kp), lo in [Kp, 2Kp), zero
-// padded, every element written on every call.
-__global__ void static_split_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ x2,
-                                    int64_t M, int64_t K, int64_t Kp) {
-  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= M * Kp) return;
-  int64_t m = idx / Kp, k = idx - m * Kp;
-  float v = k < K ? x[m * K + k] : 0.0f;
-  __nv_bfloat16 hi = __float2bfloat16_rn(v);
-  __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-  x2[m * 2 * Kp + k] = hi;
-  x2[m * 2 * Kp + Kp + k] = lo;
-}
-
 }  // namespace
 }  // namespace nk
 
@@ -98,9 +84,8 @@ extern "C" nk_status nk_gemm_w8row_f32_static(const float *x, const int8_t *wq,
   nk_status st = static_split_buffer(&buf);
   if (st != NK_OK) return st;
   cudaStream_t s = as_stream(stream);
-  static_split_kernel<<<(unsigned)ceil_div(m * kp, 256), 256, 0, s>>>(
-      x, reinterpret_cast<__nv_bfloat16 *>(buf), m, k, kp);
-  st = check_launch("static_split_kernel");
+  // the same split as the regular entry point (every byte rewritten per call)
+  st = launch_split_f32(x, m, k, kp, reinterpret_cast<uint16_t *>(buf), s);
   if (st != NK_OK) return st;
 
   const int bn = m <= 64 ? 64 : 256;

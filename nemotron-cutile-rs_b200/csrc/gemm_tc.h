@@ -18,4 +18,10 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
                   const uint16_t *x, int64_t x_rows, int64_t x_k, int64_t ldx_elems, int bn,
                   TcArgs args, int grid, cudaStream_t stream, int pair = 1, int fa = 1);
 
+// f32 activations [m, k] -> bf16 hi | lo halves [m, 2*kp] (kp = ceil(k/64)*64,
+// zero padded; every element written), the operand of the f32-activation
+// projections: hi + lo carries the top 16 significand bits of each value.
+nk_status launch_split_f32(const float *x, int64_t m, int64_t k, int64_t kp, uint16_t *x2,
+                           cudaStream_t stream);
+
 }  // namespace nk

@@ -70,9 +70,11 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
 // Defined in common.cu; other units get its device address from device_error_ptr().
 int *device_error_ptr();  // current device's error word (device address)
 
-// Per-device library scratch (grown on demand, never shrunk).  Used for
-// reduction flags and small staging buffers of the API calls.
+// Library scratch of the calling (device, stream) pair, grown on demand and
+// never shrunk (nk_scratch_release frees it): split-K partial sums, reduction
+// flags and staging buffers of the API calls that take no workspace argument.
 nk_status scratch(size_t bytes, void **ptr, cudaStream_t stream);
+nk_status release_scratch(cudaStream_t stream);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

@@ -33,7 +33,7 @@ STATUS_NAMES = {
 F32, BF16 = 0, 1
 EPI_RELU2 = 1
 ROUTE_SIGMOID, ROUTE_SOFTMAX, ROUTE_SIGMOID_RENORM = 0, 1, 2
-W_BF16, W_INT8_ROW = 0, 1
+W_BF16, W_INT8_ROW, W_INT4_AFFINE = 0, 1, 2
 
 _c = ctypes
 _sz = _c.c_size_t
@@ -119,6 +119,13 @@ _SIGS = {
     "nk_gemm_w8row": (_i32, [_p, _i32, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
     "nk_gemm_w8row_f32_static": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
     "nk_gemm_w4a": (_i32, [_p, _i32, _p, _sz, _f, _u32, _p, _p, _i32, _i64, _i64, _i64, _i32, _p]),
+    "nk_gemm_workspace_bytes": (_i32, [_i32, _i32, _i64, _i64, _i64, _p]),
+    "nk_gemm_bf16_ws": (_i32, [_p, _i32, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p, _sz, _p]),
+    "nk_gemm_w8row_ws": (_i32, [_p, _i32, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i32, _p, _sz,
+                                _p]),
+    "nk_gemm_w4a_ws": (_i32, [_p, _i32, _p, _sz, _f, _u32, _p, _p, _i32, _i64, _i64, _i64, _i32,
+                              _p, _sz, _p]),
+    "nk_scratch_release": (_i32, [_p]),
     "nk_pack_int4": (_i32, [_p, _sz, _p, _sz, _p]),
     "nk_unpack_int4": (_i32, [_p, _sz, _sz, _p, _sz, _p]),
     "nk_quantize_int4": (_i32, [_p, _sz, _f, _u32, _p, _sz, _p]),
@@ -261,13 +268,26 @@ def gemm_f32(lhs, rhs, m: int, k: int, n: int, out=None, stream=None):
     return out
 
 
+def gemm_workspace_bytes(kind: str, x_dtype, m: int, k: int, n: int) -> int:
+    """nk_gemm_workspace_bytes: scratch the *_ws projections need for this shape."""
+    import torch
+
+    wk = {"bf16": W_BF16, "int8": W_INT8_ROW, "int4": W_INT4_AFFINE}[kind]
+    b = ctypes.c_size_t(0)
+    call("nk_gemm_workspace_bytes", wk, F32 if x_dtype == torch.float32 else BF16, m, k, n,
+         ctypes.byref(b))
+    return b.value
+
+
 def gemm(x, w, *, kind: str = "bf16", bias=None, scales=None, scale: float = 1.0,
          zero_point: int = 0, n: int | None = None, out_dtype=None, relu2: bool = False,
-         stream=None):
+         stream=None, workspace=None):
     """Projection Y[M,N] = X[M,K]·Wᵀ (+bias) (relu2) — LinearProjection::project_into.
 
     kind: "bf16" (w bf16 [N,K]), "int8" (w int8 [N,K], scales f32 [N]),
     "int4" (w uint8 packed reference layout [K,N], scale/zero_point).
+    workspace: optional uint8 device tensor of >= gemm_workspace_bytes (the
+    *_ws entry points); by default the library's per-stream scratch.
     """
     import torch
 
@@ -283,6 +303,20 @@ def gemm(x, w, *, kind: str = "bf16", bias=None, scales=None, scale: float = 1.0
     y_dtype = F32 if out_dtype == torch.float32 else BF16
     flags = EPI_RELU2 if relu2 else 0
     s = stream_ptr(stream)
+    if workspace is not None:
+        wsp, wsn = ptr(workspace), workspace.numel()
+        if kind == "bf16":
+            call("nk_gemm_bf16_ws", ptr(x), x_dtype, ptr(w), ptr(bias), ptr(y), y_dtype, m, k, n,
+                 flags, wsp, wsn, s)
+        elif kind == "int8":
+            call("nk_gemm_w8row_ws", ptr(x), x_dtype, ptr(w), ptr(scales), ptr(bias), ptr(y),
+                 y_dtype, m, k, n, flags, wsp, wsn, s)
+        elif kind == "int4":
+            call("nk_gemm_w4a_ws", ptr(x), x_dtype, ptr(w), w.numel(), float(scale),
+                 int(zero_point), ptr(bias), ptr(y), y_dtype, m, k, n, flags, wsp, wsn, s)
+        else:
+            raise ValueError(kind)
+        return y
     if kind == "bf16":
         call("nk_gemm_bf16", ptr(x), x_dtype, ptr(w), ptr(bias), ptr(y), y_dtype, m, k, n, flags, s)
     elif kind == "int8":

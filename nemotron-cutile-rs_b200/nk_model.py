@@ -93,6 +93,8 @@ class Decoder:
         def randn(*shape, std=cfg.std, dtype=torch.bfloat16):
             return (torch.randn(*shape, device=device, generator=g) * std).to(dtype)
 
+        randn.uniform = lambda *shape: torch.rand(*shape, device=device, generator=g)
+
         H = cfg.hidden
         w = weights or {}
         self.embed = w.get("embed", randn(cfg.vocab, H, std=1.0))
@@ -121,7 +123,7 @@ class Decoder:
         lw = lw or dict(
             w_in=randn(W, c.hidden), w_out=randn(c.hidden, C),
             conv=randn(C, c.conv_kernel, std=0.5, dtype=torch.float32),
-            a=-(0.5 + torch.rand(c.mamba_heads, device=self.dev)),
+            a=-(0.5 + randn.uniform(c.mamba_heads)),
             d=randn(c.mamba_heads, std=1.0, dtype=torch.float32),
             norm=1.0 + randn(C, std=0.1, dtype=torch.float32))
         blk = nk_mamba.Mamba2Block(lw["w_in"], lw["w_out"], lw["conv"], lw["a"], lw["d"],
