@@ -113,13 +113,20 @@ def make_weights(torch, nk, dev, kind, seed=1234):
     router = randn(E, H, std=0.02)
     w = nk.MoeWeights(hidden=H, experts=E, top_k=K, inter=I, shared_inter=IS,
                       route_mode=nk.ROUTE_SIGMOID_RENORM,
-                      weight_kind=nk.W_BF16 if kind == "bf16" else nk.W_INT8_ROW,
+                      weight_kind={"bf16": nk.W_BF16, "int8": nk.W_INT8_ROW,
+                                   "int4": nk.W_INT4_AFFINE}[kind],
                       router_w3=nk.router_split(router))
     shapes = {"up": (E, I, H), "down": (E, H, I), "shared_up": (IS, H), "shared_down": (H, IS)}
     for name, shp in shapes.items():
         f = randn(*shp, std=0.02).to(torch.bfloat16)
         if kind == "bf16":
             setattr(w, f"{name}_w", f)
+        elif kind == "int4":  # the reference's INT4-affine format, one scale per expert
+            codes, sc, zp, _ = nk.quantize_int4_experts(f.reshape(-1, *shp[-2:]))
+            setattr(w, f"{name}_w", codes if len(shp) == 3 else codes[0])
+            setattr(w, f"{name}_scale", sc)
+            setattr(w, f"{name}_zero_point", zp)
+            del f
         else:
             q, s = nk.quantize_int8_row(f.float().reshape(-1, shp[-1]))
             setattr(w, f"{name}_w", q.reshape(shp))
@@ -130,18 +137,20 @@ def make_weights(torch, nk, dev, kind, seed=1234):
 
 
 # ---------------------------------------------------------------- cpu side
-def cpu_sample(weights_np, x_np, tokens, threads, orc):
+def cpu_sample(weights_np, x_np, tokens, threads, orc, outputs=None):
     """Oracle MoE (the reference's algorithm, gathered rows) over `tokens` rows
-    split across `threads` host threads; returns seconds."""
+    split across `threads` host threads; returns seconds.  outputs: a dict
+    that receives "out" [tokens, H] and "idx" [tokens, k]."""
     from concurrent.futures import ThreadPoolExecutor
 
     chunks = [c for c in _split(tokens, threads) if c[1] > c[0]]
+    res = {}
 
     def run(c):
         a, b = c
-        orc.moe(H, E, K, I, IS, weights_np["router_kn"], None, weights_np["up_kn"], None,
-                weights_np["down_kn"], None, weights_np["sup_kn"], None, weights_np["sdown_kn"],
-                None, x_np[a:b], b - a, orc.SIGMOID_RENORM)
+        res[a] = orc.moe(H, E, K, I, IS, weights_np["router_kn"], None, weights_np["up_kn"],
+                         None, weights_np["down_kn"], None, weights_np["sup_kn"], None,
+                         weights_np["sdown_kn"], None, x_np[a:b], b - a, orc.SIGMOID_RENORM)
 
     t0 = time.perf_counter()
     if len(chunks) == 1:
@@ -149,7 +158,48 @@ def cpu_sample(weights_np, x_np, tokens, threads, orc):
     else:
         with ThreadPoolExecutor(len(chunks)) as ex:
             list(ex.map(run, chunks))
-    return time.perf_counter() - t0
+    dt = time.perf_counter() - t0
+    if outputs is not None:
+        import numpy as np
+
+        outputs["out"] = np.concatenate([res[c[0]][0].reshape(-1, H) for c in chunks])
+        outputs["idx"] = np.concatenate([res[c[0]][1].reshape(-1, K) for c in chunks])
+    return dt
+
+
+def cpu_as_written(weights_np, x_np, rows, threads, orc):
+    """MoeLayer::forward_into as the reference computes it (moe.rs:195-246): every
+    expert selected anywhere in the batch runs its MLP over ALL the batch's rows;
+    at T = 4096 tokens all 128 experts are selected, so per token that is the
+    router, 128 expert MLPs and the shared expert.  Times that work for `rows`
+    tokens (the 128 expert MLPs over the rows, split over `threads`); returns
+    seconds per token."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    xs = x_np[:rows]
+
+    def expert(e):
+        orc.mlp(H, I, weights_np["up_kn"][e], None, weights_np["down_kn"][e], None, xs, rows)
+
+    t0 = time.perf_counter()
+    orc.linear(weights_np["router_kn"], None, H, E, xs, rows)
+    orc.mlp(H, IS, weights_np["sup_kn"], None, weights_np["sdown_kn"], None, xs, rows)
+    with ThreadPoolExecutor(max(threads, 1)) as ex:
+        list(ex.map(expert, range(E)))
+    return (time.perf_counter() - t0) / rows
+
+
+def cpu_info():
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count()}
 
 
 def _split(n, parts):
@@ -202,9 +252,11 @@ class L2Flush:
         self.torch.sum(self.r, dim=0, out=self.acc)
 
 
-def gemm_sweep(torch, nk, dev, reps=5):
-    """Benchmark config 2: Y = X·Wᵀ, bf16 and int8-per-row weights, per shape the
-    mean of `reps` CUDA-event timings of a graph replay with an L2 flush before
+def gemm_sweep(torch, nk, dev, reps=5, ms=(1, 16, 128, 2048, 8192), cublas=True):
+    """Benchmark config 2: Y = X·Wᵀ over (K,N) in {(4096,4096), (4096,21504),
+    (21504,4096)} and the given M, with bf16, int8-per-row and the reference's
+    INT4-affine weights (nk_gemm_w4a, [K,N] nibble layout); per shape the mean
+    of `reps` CUDA-event timings of a graph replay with an L2 flush before
     each; cuBLAS (torch.matmul, bf16) timed the same way for context."""
     pk = peaks()
     flush = L2Flush(torch, dev)
@@ -216,10 +268,12 @@ def gemm_sweep(torch, nk, dev, reps=5):
         (after a warm-up call that sizes libnk's scratch) and the graph is
         replayed, so host-side launch overhead is excluded for both libnk and
         cuBLAS."""
-        fn()
+        side = torch.cuda.Stream()
+        with torch.cuda.stream(side):  # libnk's scratch is per stream: warm up on
+            fn()                        # the stream the capture uses
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph, stream=side):
             fn()
         ts = []
         for _ in range(reps + 1):
@@ -232,26 +286,62 @@ def gemm_sweep(torch, nk, dev, reps=5):
             ts.append(a.elapsed_time(b_))
         return sum(ts[1:]) / reps
 
+    def entry(ms_, flops, bytes_):
+        return {"us": round(ms_ * 1e3, 2), "tflops": round(flops / ms_ / 1e9, 1),
+                "gbs": round(bytes_ / ms_ / 1e6, 1),
+                "tensor_frac": round(flops / ms_ / 1e9 / pk["bf16_tflops"], 3),
+                "hbm_frac": round(bytes_ / ms_ / 1e6 / pk["hbm_gbs"], 3)}
+
     for (k, n) in [(4096, 4096), (4096, 21504), (21504, 4096)]:
         w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         q, s = nk.quantize_int8_row(w.float())
-        for m in (1, 16, 128, 2048, 8192):
+        _, s4, _, p4 = nk.quantize_int4_experts(w.reshape(1, n, k))  # reference [K,N] codes
+        p4, s4 = p4[0], float(s4[0].item())
+        for m in ms:
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
             row = {"m": m, "k": k, "n": n}
             flops = 2 * m * n * k
-            for kind, wb, fn in (
-                    ("bf16", 2, lambda: nk.gemm(x, w, out_dtype=torch.bfloat16)),
-                    ("int8", 1, lambda: nk.gemm(x, q, kind="int8", scales=s,
-                                                out_dtype=torch.bfloat16)),
-                    ("cublas_bf16", 2, lambda: torch.matmul(x, w.t()))):
-                ms = timed(fn)
+            kinds = [("bf16", 2, lambda: nk.gemm(x, w, out_dtype=torch.bfloat16)),
+                     ("int8", 1, lambda: nk.gemm(x, q, kind="int8", scales=s,
+                                                 out_dtype=torch.bfloat16)),
+                     ("int4", 0.5, lambda: nk.gemm(x, p4, kind="int4", scale=s4, zero_point=8,
+                                                   n=n, out_dtype=torch.bfloat16))]
+            if cublas:
+                kinds.append(("cublas_bf16", 2, lambda: torch.matmul(x, w.t())))
+            for kind, wb, fn in kinds:
                 bytes_ = wb * n * k + 2 * m * k + 2 * m * n
-                row[kind] = {"us": round(ms * 1e3, 2), "tflops": round(flops / ms / 1e9, 1),
-                             "gbs": round(bytes_ / ms / 1e6, 1),
-                             "tensor_frac": round(flops / ms / 1e9 / pk["bf16_tflops"], 3),
-                             "hbm_frac": round(bytes_ / ms / 1e6 / pk["hbm_gbs"], 3)}
+                row[kind] = entry(timed(fn), flops, bytes_)
             res.append(row)
     return res
+
+
+def config1_linear(torch, nk, dev, reps=20):
+    """Benchmark config 1 at its own size and seed: X f32 [64, 2048] ~ N(0,1),
+    W [2048, 2048] ~ N(0, 0.02) quantized int8 per output row, Y = X·dequant(W)ᵀ
+    through nk_gemm_w8row with f32 activations (CUDA events, L2 flushed)."""
+    pk = peaks()
+    flush = L2Flush(torch, dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    m, k, n = 64, 2048, 2048
+    x = torch.randn(m, k, device=dev, generator=g)
+    q, s = nk.quantize_int8_row(torch.randn(n, k, device=dev, generator=g) * 0.02)
+    nk.gemm(x, q, kind="int8", scales=s)
+    ts = []
+    for _ in range(reps + 1):
+        flush()
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        nk.gemm(x, q, kind="int8", scales=s)
+        b_.record()
+        b_.synchronize()
+        ts.append(a.elapsed_time(b_))
+    ms_ = sum(ts[1:]) / reps
+    bytes_ = 4 * m * k + n * k + 4 * n + 4 * m * n
+    return {"config": "benchmark config 1: int8 per-row weights, f32 X [64, 2048], "
+                      "W [2048, 2048], seed 0 (eager call incl. launch)",
+            "us": round(ms_ * 1e3, 2), "gbs": round(bytes_ / ms_ / 1e6, 1),
+            "hbm_frac": round(bytes_ / ms_ / 1e6 / pk["hbm_gbs"], 3),
+            "gflops": round(2 * m * n * k / ms_ / 1e6, 1)}
 
 
 def tp_projections(torch, dev, world, reps=10):
@@ -478,6 +568,73 @@ class EpTimer:
         return out
 
 
+# ---------------------------------------------------------------- profiling cases
+# `bench.py --case NAME ...` runs one libnk path alone (only what its kernels
+# need on the device) and prints one line of CUDA-event timings: the small,
+# self-contained commands the ncu summaries under profiles/ were taken with.
+def _case_timed(torch, fn, warmup, iters):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / max(iters, 1)
+
+
+def case_mamba_block(args, torch, nk):
+    import nk_mamba
+
+    H, P, G, S, K, hid = 128, 64, 8, 128, 4, 4096
+    C = H * P
+    W = 2 * C + 2 * G * S + H
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w_in = (torch.randn(W, hid, device="cuda", generator=g) * 0.02).bfloat16()
+    w_out = (torch.randn(hid, C, device="cuda", generator=g) * 0.02).bfloat16()
+    conv = torch.randn(C, K, device="cuda", generator=g) * 0.5
+    a = -torch.rand(H, device="cuda", generator=g) - 0.5
+    d = torch.randn(H, device="cuda", generator=g)
+    nw = torch.randn(C, device="cuda", generator=g)
+    blk = nk_mamba.Mamba2Block(w_in, w_out, conv, a, d, nw, heads=H, head_dim=P, groups=G,
+                               state=S, kernel_size=K, parallel=False)
+    x = torch.randn(args.tokens, hid, device="cuda", generator=g).bfloat16()
+    ms = _case_timed(torch, lambda: blk.forward(x, 1, args.tokens), args.warmup, args.iters)
+    print(f"mamba_block tokens={args.tokens}: {ms:.3f} ms per forward")
+
+
+def case_attention(args, torch, nk):
+    B, Sq, Hq, Hkv, d = args.batch, args.q_seq, 32, 2, 128
+    L = args.kv_len or Sq
+    cache = nk.KvCache(B, Hkv, d, ((L + 63) // 64) * 64)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    kv = torch.randn(B * L, Hkv * d, device="cuda", generator=g).bfloat16()
+    cache.append(kv, kv, L)
+    q = torch.randn(B * Sq, Hq * d, device="cuda", generator=g).bfloat16()
+    ws = [None]
+
+    def run():
+        o, ws[0] = nk.attention_gqa(q, cache, Sq, Hq, causal=True, workspace=ws[0])
+
+    ms = _case_timed(torch, run, args.warmup, args.iters)
+    print(f"attention batch={B} q_seq={Sq} kv_len={L}: {ms:.3f} ms per call")
+
+
+def case_gemm(args, torch, nk):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(args.m, args.k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(args.n, args.k, device="cuda", generator=g) * 0.02).bfloat16()
+    ms = _case_timed(torch, lambda: nk.gemm(x, w, out_dtype=torch.bfloat16), args.warmup, args.iters)
+    print(f"gemm m={args.m} k={args.k} n={args.n}: {ms * 1e3:.1f} us per call "
+          f"(back to back, weights L2-resident when they fit)")
+
+
+PROFILE_CASES = {"mamba_block": "case_mamba_block", "attention": "case_attention",
+                 "gemm": "case_gemm"}
+
+
 # ---------------------------------------------------------------- arms
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -499,11 +656,9 @@ def reference_arm(args):
     total = sum(secs)
     value = n_tok * args.steps / total
     # MoeLayer::forward_into as written runs every selected expert over all T
-    # rows (moe.rs:195-246): with all 128 experts selected at T = 4096 that is
-    # E·T row-MLPs instead of the T·k gathered ones.  Its rate, scaled by the
-    # FLOP ratio from the gathered timing above:
-    routed, shared, router = layer_flops(T)
-    dense_ratio = (routed * E / K + shared + router) / (routed + shared + router)
+    # rows (moe.rs:195-246): timed on a small row sample, rate per token.
+    aw_rows = max(2, min(8, threads))
+    aw_per_tok = cpu_as_written(wnp, x, aw_rows, threads, orc)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -511,15 +666,17 @@ def reference_arm(args):
         "vs_baseline": None, "dtype": "f32/f64-accumulate", "data": "synthetic",
         "config": config_dict(args, "reference"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": min(threads, n_tok),
-                         "kind": "port",
+                         "kind": "port", **cpu_info(),
                          "sample": f"{n_tok} of {T} tokens per step, the reference's MoE host "
-                                   "algorithm (oracle/nk_oracle.c, gathered rows) over "
-                                   f"{min(threads, n_tok)} threads",
-                         "as_written_estimate": {
-                             "value": value / dense_ratio, "unit": "tokens/s",
-                             "note": "every selected expert over all tokens, as moe.rs:195-246 "
-                                     f"computes it: the gathered rate / {dense_ratio:.1f} "
-                                     "(FLOP ratio), not timed"}},
+                                   "algorithm (oracle/nk_oracle.c, gathered rows: each token "
+                                   f"through its {K} experts) over {min(threads, n_tok)} threads",
+                         "as_written": {
+                             "value": 1.0 / aw_per_tok, "unit": "tokens/s",
+                             "cores": threads,
+                             "sample": f"timed: {aw_rows} tokens through the router, all {E} "
+                                       "expert MLPs and the shared expert, as moe.rs:195-246 "
+                                       f"computes a {T}-token batch (every selected expert over "
+                                       "all rows; all 128 are selected at this batch size)"}},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -693,7 +850,7 @@ def nk_arm(args):
     tp_result = tp_projections(torch, dev, world) if args.tp else None
     if rank == 0:
         pk = peaks()
-        wbytes_per = 1 if args.weights == "int8" else 2
+        wbytes_per = {"bf16": 2, "int8": 1, "int4": 0.5}[args.weights]
         if world == 1:
             counts = np.bincount(idx.cpu().numpy(), minlength=E)
             active = int((counts > 0).sum())
@@ -722,7 +879,7 @@ def nk_arm(args):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if args.weights == "bf16" else "bf16 activations, int8 weights",
+            "dtype": "bf16" if args.weights == "bf16" else f"bf16 activations, {args.weights} weights",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
             "config": config_dict(args, "nk"),
             "tflops": (routed + shared + router) * world * args.steps / (total_ms / 1e3) / 1e12,
@@ -750,11 +907,15 @@ def nk_arm(args):
             # dispatch and return instead)
             "gpu_launches": (13 if world == 1 else 15) * args.steps * 2,
         }
-        line["config"]["e2e"] = (
+        line["e2e"]["how"] = (
             "nk_moe_pipeline_submit per step (host-buffer executor: pinned x in, f32 out back; "
             "copies of adjacent steps overlap the forward; no L2 flush: each step streams "
             "all routed experts' weights, 1.3-2.6 GB > L2)"
             if world == 1 else "copy in, forward, copy out back to back per step")
+        if world == 1 and not args.no_gemm_rows:
+            line["config1_linear"] = config1_linear(torch, nk, dev)
+            line["config2_gemm_rows"] = gemm_sweep(torch, nk, dev, ms=(1, 16, 128, 8192),
+                                                   cublas=False)
         if args.tp:
             line["tp_projections"] = tp_result
         if args.e2e and world == 1:
@@ -768,13 +929,26 @@ def nk_arm(args):
             wnp = host_weights_from_device(torch, w, ref["router"])
             xs = x[:64].float().cpu().numpy()
             n_tok, _ = calibrate_tokens(lambda n: cpu_sample(wnp, xs, n, 1, orc), 15.0, 64)
-            secs = cpu_sample(wnp, xs, n_tok, 1, orc)
+            outs = {}
+            secs = cpu_sample(wnp, xs, n_tok, 1, orc, outputs=outs)
+            # the sample doubles as a parity check of the timed GPU forward
+            gi = idx.reshape(T, K)[:n_tok].cpu().numpy()
+            go = out[:n_tok].cpu().numpy()
+            routes_equal = bool(np.array_equal(gi, outs["idx"]))
+            rel = float(np.max(np.abs(go - outs["out"])) / np.max(np.abs(outs["out"])))
+            assert routes_equal and rel <= 2e-2, (routes_equal, rel)
+            aw_per_tok = cpu_as_written(wnp, xs, 2, 1, orc)
             line["cpu_baseline"] = {
                 "value": n_tok / secs, "unit": "tokens/s", "cores": 1, "kind": "port",
+                **cpu_info(),
                 "sample": f"{n_tok} of {T} tokens: oracle/nk_oracle.c restatement of "
                           "MoeLayer::forward_into (f64-accumulate GEMM loops) on the GPU arm's "
-                          "weights, single thread, gathered rows (the reference itself runs "
-                          "every selected expert over all rows)"}
+                          "weights, single thread, gathered rows",
+                "agrees_with_gpu": {"routes_equal": routes_equal, "max_rel_err": rel},
+                "as_written": {"value": 1.0 / aw_per_tok, "unit": "tokens/s", "cores": 1,
+                               "sample": "timed: 2 tokens through the router, all 128 expert "
+                                         "MLPs and the shared expert (moe.rs:195-246 at a "
+                                         "4096-token batch)"}}
         print_json(line)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -798,8 +972,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["nk", "reference"], default="nk")
-    ap.add_argument("--weights", choices=["bf16", "int8"], default="bf16")
+    ap.add_argument("--weights", choices=["bf16", "int8", "int4"], default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm-rows", action="store_true",
+                    help="skip the config-1 and config-2 projection rows of the default line")
     ap.add_argument("--tokens", type=int, default=T,
                     help="tokens per GPU (profiling captures use a smaller case)")
     ap.add_argument("--experts", type=int, default=E)
@@ -816,7 +992,23 @@ def main():
     ap.add_argument("--graph", action="store_true",
                     help="replay the forward as a captured CUDA graph (measured no faster "
                          "than eager launches: the step is device-bound)")
+    ap.add_argument("--case", choices=sorted(PROFILE_CASES),
+                    help="run one libnk path alone for profiling (see the profiles/ commands)")
+    ap.add_argument("--iters", type=int, default=3, help="--case: timed calls")
+    ap.add_argument("--batch", type=int, default=8, help="--case attention")
+    ap.add_argument("--q-seq", type=int, default=1024, help="--case attention")
+    ap.add_argument("--kv-len", type=int, default=0, help="--case attention")
+    ap.add_argument("--m", type=int, default=1, help="--case gemm")
+    ap.add_argument("--k", type=int, default=4096, help="--case gemm")
+    ap.add_argument("--n", type=int, default=21504, help="--case gemm")
     args = ap.parse_args()
+    if args.case:
+        import torch
+
+        import nk
+
+        globals()[PROFILE_CASES[args.case]](args, torch, nk)
+        return 0
     globals()["T"], globals()["E"] = args.tokens, args.experts
     if args.warmup < 3:
         args.warmup = 3

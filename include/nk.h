@@ -272,16 +272,17 @@ typedef struct nk_moe_layer {
   int64_t inter;         /* I, routed expert width */
   int64_t shared_inter;  /* Is, 0 = no shared expert */
   int32_t route_mode;    /* NK_ROUTE_* */
-  int32_t weight_kind;   /* NK_W_BF16 or NK_W_INT8_ROW (experts and shared expert) */
+  int32_t weight_kind;   /* NK_W_BF16, NK_W_INT8_ROW or NK_W_INT4_AFFINE (experts and
+                            shared expert) */
   const uint16_t *router_w3; /* [E, 3*Hp] bf16, Hp = ceil(H/64)*64: the f32 router weight
                                 [E,H] split exactly into three zero-padded bf16 parts
                                 (nk_router_split); scores carry f32 accuracy */
   const float *router_b;     /* [E] or NULL */
-  const void *up_w;          /* [E, I, H] */
-  const float *up_scale;     /* [E, I] (INT8_ROW) */
+  const void *up_w;          /* [E, I, H]; INT4_AFFINE: codes [E, I, H/2] (nk_int4_kn_to_nk) */
+  const float *up_scale;     /* [E, I] (INT8_ROW); [E] per-expert scale (INT4_AFFINE) */
   const float *up_b;         /* [E, I] or NULL */
-  const void *down_w;        /* [E, H, I] */
-  const float *down_scale;   /* [E, H] (INT8_ROW) */
+  const void *down_w;        /* [E, H, I]; INT4_AFFINE: codes [E, H, I/2] */
+  const float *down_scale;   /* [E, H] (INT8_ROW); [E] (INT4_AFFINE) */
   const float *down_b;       /* [E, H] or NULL */
   const void *shared_up_w;   /* [Is, H] */
   const float *shared_up_scale;
@@ -289,6 +290,12 @@ typedef struct nk_moe_layer {
   const void *shared_down_w; /* [H, Is] */
   const float *shared_down_scale;
   const float *shared_down_b;
+  /* INT4_AFFINE zero points (quantize.rs:180-186 params, one per expert):
+   * W = (code - zero_point) * scale, dequantized inside the GEMMs. */
+  const uint8_t *up_zero_point;          /* [E] */
+  const uint8_t *down_zero_point;        /* [E] */
+  const uint8_t *shared_up_zero_point;   /* [1] */
+  const uint8_t *shared_down_zero_point; /* [1] */
 } nk_moe_layer;
 
 /* Splits a router weight f32 [E,H] into the [E, 3*Hp] bf16 triple used by
@@ -301,6 +308,14 @@ nk_status nk_router_split(const float *router_w, int64_t experts, int64_t hidden
  * linear.rs:324) into the [N,K] bf16 layout the GEMMs read. */
 nk_status nk_linear_pack_kn(const float *w_kn, int64_t k, int64_t n, uint16_t *w_nk,
                             void *stream);
+
+/* Repacks INT4 codes from the reference's [K,N] nibble layout (quantize.rs:
+ * flat index k*N + n in byte index/2, low nibble for even index; each of the
+ * `batch` matrices ceil(K*N/2) bytes, back to back) into the feature-major
+ * layout NK_W_INT4_AFFINE expert weights use: [N, K/2] bytes, byte n*K/2 + k/2,
+ * low nibble for even k (batch * N * K/2 bytes).  k even. */
+nk_status nk_int4_kn_to_nk(const uint8_t *packed_kn, int64_t batch, int64_t k, int64_t n,
+                           uint8_t *packed_nk, void *stream);
 
 /* Device workspace (bytes) nk_moe_forward needs for `tokens` rows. */
 nk_status nk_moe_workspace_bytes(const nk_moe_layer *layer, int64_t tokens, size_t *bytes);
@@ -452,6 +467,57 @@ nk_status nk_ep_return_segments(const uint16_t *expert_rows, int64_t hidden, int
                                 int32_t n_segments, const int32_t *seg_rows,
                                 const int32_t *seg_start, const int32_t *return_offset,
                                 const uint64_t *peer_out, void *stream);
+
+/* ------------------------------------------- native expert parallelism
+ * MoeLayer::forward_into (moe.rs:154-249) over G ranks, one process per GPU,
+ * the experts split evenly (rank g holds experts [g*E/G, (g+1)*E/G)); the
+ * layout the benchmark configurations ask for, not in the reference (which
+ * runs on one device, device.rs:32-54).  Every call below is issued by every
+ * rank, in the same order, on one stream per rank.
+ *
+ *   1. nk_ep_create on every rank: allocates this rank's exchange memory
+ *      (receive rows, result rows, the counts matrix, barrier flags) and
+ *      writes a handle blob of nk_ep_handle_bytes() bytes.
+ *   2. The caller gathers the blobs of all ranks, in rank order, with its own
+ *      collective (NCCL / MPI all-gather, a key-value store) and hands them to
+ *      nk_ep_connect, which maps the peers' memory (CUDA IPC).
+ *   3. nk_moe_forward_ep per layer call: routing on this rank -> per-expert
+ *      counts written into every rank's counts matrix -> device barrier ->
+ *      exchange plan -> routed rows stored straight into their expert owners'
+ *      receive buffers over NVLink -> barrier -> this rank's grouped experts
+ *      -> results stored straight back -> barrier -> shared expert (on a side
+ *      stream meanwhile) + combine in rank order.  No host synchronisation,
+ *      no library collective; the barriers are flag words in peer memory,
+ *      each wait bounded (NK_TIMEOUT in nk_device_status when a peer does not
+ *      arrive within 2 s).  Plain peer loads and stores only (no multicast).
+ *   4. nk_ep_destroy after every rank has finished its last forward (for
+ *      example after nk_ep_barrier and a stream synchronisation).
+ *
+ * capacity_rows: receive rows per rank (0: the worst case ranks * max_tokens
+ * * top_k); a forward that routes more rows to one rank reports
+ * NK_WORKSPACE_TOO_SMALL through nk_device_status and drops the excess. */
+typedef struct nk_ep_ctx nk_ep_ctx;
+size_t nk_ep_handle_bytes(void);
+nk_status nk_ep_create(int32_t ranks, int32_t rank, int64_t experts, int64_t hidden,
+                       int64_t top_k, int64_t max_tokens, int64_t capacity_rows,
+                       nk_ep_ctx **out, void *handle_blob);
+nk_status nk_ep_connect(nk_ep_ctx *ctx, const void *all_blobs);
+/* layer: the whole layer (router over all E experts, shared expert); local:
+ * this rank's E/G experts stacked in local order (same kind and widths; int8
+ * / INT4 scales and zero points sliced to the local experts). */
+nk_status nk_moe_forward_ep_workspace_bytes(const nk_ep_ctx *ctx, const nk_moe_layer *layer,
+                                            const nk_moe_layer *local, int64_t tokens,
+                                            size_t *bytes);
+nk_status nk_moe_forward_ep(nk_ep_ctx *ctx, const nk_moe_layer *layer, const nk_moe_layer *local,
+                            const uint16_t *x, int64_t tokens, void *out, int32_t out_dtype,
+                            int32_t *indices, float *weights, void *workspace,
+                            size_t workspace_bytes, void *stream);
+/* A device barrier across the ranks on `stream` (bounded like the others). */
+nk_status nk_ep_barrier(nk_ep_ctx *ctx, void *stream);
+/* Rows this rank received in the last forward (device int32, copied on the
+ * legacy stream). */
+nk_status nk_ep_received_rows(const nk_ep_ctx *ctx, int32_t *rows_device);
+nk_status nk_ep_destroy(nk_ep_ctx *ctx);
 
 /* ---------------------------------------------------------------- tracing */
 

@@ -241,7 +241,7 @@ static ProjPlan plan_projection(int wk, bool aligned, int x_dtype, int64_t m, in
     p.w_period = (int)(p.kp / 64);
     p.k_blocks = 2 * p.w_period;
   }
-  p.bn = m <= 64 ? 64 : 256;
+  p.bn = m <= 16 ? 16 : (m <= 64 ? 64 : 256);
   const int f_tiles = (int)ceil_div(n, 128), t_tiles = (int)ceil_div(m, p.bn);
   const double w_bytes = (double)n * (double)k * (wk == WK_BF16 ? 2.0 : wk == WK_INT8 ? 1.0 : 0.5);
   int splits = choose_k_splits(f_tiles, t_tiles, p.k_blocks, num_sms(), w_bytes, m, n);

@@ -88,7 +88,7 @@ extern "C" nk_status nk_gemm_w8row_f32_static(const float *x, const int8_t *wq,
   st = launch_split_f32(x, m, k, kp, reinterpret_cast<uint16_t *>(buf), s);
   if (st != NK_OK) return st;
 
-  const int bn = m <= 64 ? 64 : 256;
+  const int bn = m <= 16 ? 16 : (m <= 64 ? 64 : 256);
   TcArgs a{};
   a.f_tiles = (int)ceil_div(n, 128);
   a.t_tiles = (int)ceil_div(m, bn);

@@ -39,6 +39,19 @@ __device__ __forceinline__ void load_tile(const TcArgs &a, int t, TcTile &tile, 
   tile.valid = ((fv > FH ? FH : fv) << 16) | (tv > BN ? BN : tv);
 }
 
+// K blocks in the raw group that starts at tile-relative block kk: up to G,
+// not past the tile's K range, and not across the weight K period (f32
+// activations read every weight K block twice, hi then lo).
+__device__ __forceinline__ int raw_group_len(int G, int kk, int k_begin, int k_count,
+                                             int w_period) {
+  int len = G < k_count - kk ? G : k_count - kk;
+  if (w_period > 0) {
+    const int to_wrap = w_period - (k_begin + kk) % w_period;
+    if (to_wrap < len) len = to_wrap;
+  }
+  return len;
+}
+
 __device__ __forceinline__ uint32_t mma_n(int t_valid, int bn) {
   uint32_t n = (uint32_t)((t_valid + 15) & ~15);
   if (n < 16) n = 16;
@@ -56,18 +69,20 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
   constexpr int S = Cfg::kStages;
   constexpr int FH = Cfg::kFeatRows;
   constexpr bool kQuant = WK != WK_BF16;
+  constexpr int R = Cfg::kRawSlots > 0 ? Cfg::kRawSlots : 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *a_tiles = smem;                          // S x FA x 16 KB bf16 weight tiles (SW128)
   uint8_t *b_tiles = a_tiles + S * Cfg::kABytes;    // S x kBRows*128 token tiles (SW128)
-  uint8_t *raw_tiles = b_tiles + S * Cfg::kBBytes;  // S x raw weight tiles (quantized)
-  uint64_t *bars = reinterpret_cast<uint64_t *>(raw_tiles + S * Cfg::kRawBytes);
+  uint8_t *raw_tiles = b_tiles + S * Cfg::kBBytes;  // R x raw weight tiles (quantized)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(raw_tiles + Cfg::kRawSlots * Cfg::kRawTileBytes);
   uint64_t *full = bars;            // leader: stage's TMA bytes landed (both CTAs)
   uint64_t *empty = bars + S;       // MMAs finished reading the stage (every CTA)
   uint64_t *conv = bars + 2 * S;    // leader: converted weight tiles ready (both CTAs)
-  uint64_t *rawfull = bars + 3 * S; // this CTA's raw weight tile landed (quantized)
-  uint64_t *tfull = bars + 4 * S;   // accumulator set ready (kSlots, every CTA)
+  uint64_t *rawfull = bars + 3 * S; // this CTA's raw tile landed (R slots)
+  uint64_t *rawempty = rawfull + R; // the transform finished reading the raw slot (R)
+  uint64_t *tfull = rawempty + R;   // accumulator set ready (kSlots, every CTA)
   uint64_t *tempty = tfull + 2;     // leader: accumulator set drained (kSlots)
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -85,7 +100,10 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&conv[s], Cfg::kTransformThreads * PAIR);
-      mbar_init(&rawfull[s], 1);
+    }
+    for (int r = 0; r < R; ++r) {
+      mbar_init(&rawfull[r], 1);
+      mbar_init(&rawempty[r], Cfg::kTransformThreads > 0 ? Cfg::kTransformThreads : 1);
     }
     for (int b = 0; b < kSlots; ++b) {
       mbar_init(&tfull[b], 1);
@@ -131,6 +149,51 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
+      // Quantized kinds: raw tiles of G K blocks each run up to (R-1)·G K
+      // blocks ahead of the main ring, in the same (tile, K block) order; `rc`
+      // is their cursor (rc.kb: first K block of the next group to load).
+      constexpr int G = WeightTile<WK>::kGroup;
+      struct Cur {
+        int t, kb, k_begin, k_count, split;
+        TcTile tile;
+      };
+      Cur rc;
+      int rslot = 0;
+      uint32_t rphase = 0, r_mask = 0, r_parity = 0;
+      rc.t = cluster_id;
+      rc.kb = 0;
+      if (kQuant && rc.t < num_tiles)
+        load_tile<BN, FH>(args, rc.t, rc.tile, rc.k_begin, rc.k_count, rc.split);
+      auto issue_raw = [&]() -> bool {
+        if (!kQuant || rc.t >= num_tiles) return true;
+        if (*abort_v || !mbar_wait(&rawempty[rslot], rphase ^ 1, err)) return false;
+        const int kb = rc.k_begin + rc.kb;
+        const int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
+        const int a_row = rc.tile.w_row + (int)rank * 128;
+        uint8_t *dst = raw_tiles + rslot * Cfg::kRawTileBytes;
+        mbar_arrive_expect_tx(&rawfull[rslot], Cfg::kRawTileBytes);
+        if (WK == WK_INT8)  // [N rows, K bytes]: 128 rows x 128 bytes (2 K blocks)
+          tma_load_2d(dst, &wmap, &rawfull[rslot], wkb * 64, a_row);
+        else if (WK == WK_INT4NK)  // [N rows, K/2 bytes]: 128 rows x 128 bytes (4 K blocks)
+          tma_load_2d(dst, &wmap, &rawfull[rslot], wkb * 32, a_row);
+        else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
+          tma_load_2d(dst, &wmap, &rawfull[rslot], a_row >> 1, wkb * 64);
+        r_mask |= 1u << rslot;
+        r_parity = (r_parity & ~(1u << rslot)) | (rphase << rslot);
+        rc.kb += raw_group_len(G, rc.kb, rc.k_begin, rc.k_count, args.w_k_period);
+        if (rc.kb >= rc.k_count) {
+          rc.t += clusters;
+          rc.kb = 0;
+          if (rc.t < num_tiles)
+            load_tile<BN, FH>(args, rc.t, rc.tile, rc.k_begin, rc.k_count, rc.split);
+        }
+        if (++rslot == R) {
+          rslot = 0;
+          rphase ^= 1;
+        }
+        return true;
+      };
+      for (int j = 0; kQuant && j < R - 1 && ok; ++j) ok = issue_raw();
       for (int t = cluster_id; t < num_tiles && ok; t += clusters) {
         TcTile tile;
         int k_begin, k_count, split;
@@ -139,9 +202,10 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         const int a_row = tile.w_row + (int)rank * 128;
         const int n_a = FA == 2 && (tile.valid >> 16) > 128 ? 2 : 1;  // weight tiles loaded
         const int b_row = tile.x_row + (int)rank * (int)(n_mma / PAIR);
-        int x_map = 0;  // single CTAs: the smallest token box covering n_mma rows
-        while (PAIR == 1 && (uint32_t)token_box_rows(x_map) < n_mma) ++x_map;
+        int x_map = 0;  // the smallest token box covering this CTA's n_mma / PAIR rows
+        while ((uint32_t)token_box_rows(x_map) < n_mma / PAIR) ++x_map;
         const uint32_t x_box = token_box_rows(x_map);
+        int r_start = 0;  // first K block of the current raw group
         for (int kk = 0; kk < k_count; ++kk) {
           if (*abort_v || !mbar_wait(&empty[stage], phase ^ 1, err)) {
             ok = false;
@@ -150,27 +214,15 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
           const int kb = k_begin + kk;
           const int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
           const int xkb = args.x_k_period > 0 ? kb % args.x_k_period : kb;
-          // Token tile (and bf16 weight tile) complete on the leader's `full`;
-          // quantized raw weight tiles complete on this CTA's `rawfull`.
+          // Token tile (and bf16 weight tile) complete on the leader's `full`.
           if (leader)
             mbar_arrive_expect_tx(&full[stage],
-                                  PAIR * ((kQuant ? 0 : Cfg::kATileBytes * n_a) +
-                                          (PAIR == 2 ? Cfg::kBBytes : x_box * 128)));
-          if (kQuant) {
-            mbar_arrive_expect_tx(&rawfull[stage], Cfg::kRawTileBytes * n_a);
-            for (int ai = 0; ai < n_a; ++ai) {
-              uint8_t *dst = raw_tiles + stage * Cfg::kRawBytes + ai * Cfg::kRawTileBytes;
-              if (WK == WK_INT8)
-                tma_load_2d(dst, &wmap, &rawfull[stage], wkb * 64, a_row + ai * 128);
-              else  // INT4 [K, N/2 bytes]: 64 bytes (128 features) x 64 K rows
-                tma_load_2d(dst, &wmap, &rawfull[stage], (a_row + ai * 128) >> 1, wkb * 64);
-            }
-          }
+                                  PAIR * ((kQuant ? 0 : Cfg::kATileBytes * n_a) + x_box * 128));
           if (PAIR == 2) {
             const uint32_t fb = leader_bar(&full[stage]);
             if (!kQuant)
               tma_load_2d_pair(a_tiles + stage * Cfg::kABytes, &wmap, fb, wkb * 64, a_row);
-            tma_load_2d_pair(b_tiles + stage * Cfg::kBBytes, &xmaps.m[0], fb, xkb * 64, b_row);
+            tma_load_2d_pair(b_tiles + stage * Cfg::kBBytes, &xmaps.m[x_map], fb, xkb * 64, b_row);
           } else {
             if (!kQuant)
               for (int ai = 0; ai < n_a; ++ai)
@@ -185,16 +237,25 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
             stage = 0;
             phase ^= 1;
           }
+          if (kQuant) {  // the item ends a raw group: top the raw ring up by one group
+            if (kk == r_start + raw_group_len(G, r_start, k_begin, k_count, args.w_k_period) - 1) {
+              r_start = kk + 1;
+              if (!issue_raw()) {
+                ok = false;
+                break;
+              }
+            }
+          }
         }
       }
       if (!ok) *abort_v = 1;
       // Drain: every issued load must have landed before the CTA may exit (the
-      // leader's `full` counts both CTAs' bytes; a peer's raw tiles its own rawfull).
+      // leader's `full` counts both CTAs' bytes; raw tiles complete on this
+      // CTA's own `rawfull`).
       for (int s = 0; s < S; ++s)
-        if (issued_mask & (1u << s)) {
-          if (leader) mbar_wait(&full[s], (issued_parity >> s) & 1, err);
-          if (kQuant) mbar_wait(&rawfull[s], (issued_parity >> s) & 1, err);
-        }
+        if ((issued_mask & (1u << s)) && leader) mbar_wait(&full[s], (issued_parity >> s) & 1, err);
+      for (int r = 0; kQuant && r < R; ++r)
+        if (r_mask & (1u << r)) mbar_wait(&rawfull[r], (r_parity >> r) & 1, err);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
@@ -299,6 +360,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
       float mul = args.w_scale, add = 0.0f;
       if (frow) {
         if (args.row_scale) mul *= args.row_scale[f];
+        if (args.group_scale) mul *= args.group_scale[f / args.group_rows];
         if (args.bias) add = args.bias[f];
       }
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) +
@@ -381,58 +443,81 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
     }
   } else if (kQuant) {
     // ------------------------------------------------------------ transform
+    // Raw tile (raw ring slot) -> bf16 128-byte-swizzled weight tile (main
+    // ring stage), once the stage's previous MMAs completed.
     const int tid = threadIdx.x - 64 - Cfg::kEpiThreads;  // 0 .. kTransformThreads-1
-    int stage = 0;
-    uint32_t phase = 0;
+    constexpr int kTT = Cfg::kTransformThreads > 0 ? Cfg::kTransformThreads : 1;
+    constexpr int G = WeightTile<WK>::kGroup;
+    constexpr int RB = WeightTile<WK>::kRowBytes;  // code bytes per row per K block
+    int stage = 0, rslot = 0;
+    uint32_t phase = 0, rphase = 0;
     bool ok = true;
     for (int t = cluster_id; t < num_tiles && ok; t += clusters) {
       TcTile tile;
       int k_begin, k_count, split;
       load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
+      const int a_row = tile.w_row + (int)rank * 128;
+      int zp = args.w_zero_point;
+      if (WK == WK_INT4NK && args.group_zp) zp = (int)args.group_zp[a_row / args.group_rows];
+      const float zbias = WK == WK_INT8 ? 8388736.0f : 8388608.0f + (float)zp;  // 2^23 + bias
+      int r_start = 0, r_len = raw_group_len(G, 0, k_begin, k_count, args.w_k_period);
       for (int kb = 0; kb < k_count; ++kb) {
-        // the converted tile's slot is free once its stage's MMAs completed
-        if (*abort_v || !mbar_wait(&rawfull[stage], phase, err)) {
+        const int g = kb - r_start;  // K block within the raw tile
+        if (*abort_v || (g == 0 && !mbar_wait_backoff(&rawfull[rslot], rphase, err)) ||
+            !mbar_wait_backoff(&empty[stage], phase ^ 1, err)) {
           ok = false;
           break;
         }
-        constexpr int kTT = Cfg::kTransformThreads > 0 ? Cfg::kTransformThreads : 1;
-        const int n_a = FA == 2 && (tile.valid >> 16) > 128 ? 2 : 1;
+        const uint8_t *raw = raw_tiles + rslot * Cfg::kRawTileBytes + (WK == WK_INT4KN ? g * RB : 0);
+        uint8_t *dst = a_tiles + stage * Cfg::kABytes;
 #pragma unroll
-        for (int q = 0; q < 1024 * FA / kTT; ++q) {
-          const int ai = (q * kTT + tid) >> 10;
-          if (ai >= n_a) continue;
-          const int idx = (q * kTT + tid) & 1023;
-          const uint8_t *raw = raw_tiles + stage * Cfg::kRawBytes + ai * Cfg::kRawTileBytes;
-          uint8_t *dst = a_tiles + stage * Cfg::kABytes + ai * Cfg::kATileBytes;
-          int row, c;
+        for (int q = 0; q < 1024 / kTT; ++q) {
+          const int idx = q * kTT + tid;
+          int row, c;  // weight row (feature) and 16-byte chunk (8 K values) of it
           uint32_t packed[4];
-          if (WK == WK_INT8) {
+          if (WK == WK_INT8 || WK == WK_INT4NK) {
             row = idx >> 3;
             c = idx & 7;
-            const uint2 src = *reinterpret_cast<const uint2 *>(raw + row * 64 + c * 8);
-            // biased bytes u = v + 128 in [0, 255]; as_float(0x4B000000 | u) = 2^23 + u
-            const uint32_t w[2] = {src.x ^ 0x80808080u, src.y ^ 0x80808080u};
+            if (WK == WK_INT8) {
+              // raw rows are 128 bytes, 128-byte swizzled by TMA: 16-byte chunk j
+              // of row r sits at chunk j ^ (r & 7)
+              const int lb = g * 64 + c * 8;
+              const uint2 src = *reinterpret_cast<const uint2 *>(
+                  raw + row * 128 + ((((lb >> 4) ^ (row & 7)) << 4) | (lb & 15)));
+              // biased bytes u = v + 128 in [0, 255]; as_float(0x4B000000 | u) = 2^23 + u
+              const uint32_t w[2] = {src.x ^ 0x80808080u, src.y ^ 0x80808080u};
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const uint32_t word = w[h >> 1];
-              const int b0 = (h & 1) * 2;
-              const float lo = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 | b0)) -
-                               8388736.0f;  // 2^23 + 128
-              const float hi = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 | (b0 + 1))) -
-                               8388736.0f;
-              // exact small integers: the bf16 is the upper half of the f32
-              packed[h] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+              for (int h = 0; h < 4; ++h) {
+                const uint32_t word = w[h >> 1];
+                const int b0 = (h & 1) * 2;
+                const float lo =
+                    __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 | b0)) - zbias;
+                const float hi =
+                    __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 | (b0 + 1))) - zbias;
+                // exact small integers: the bf16 is the upper half of the f32
+                packed[h] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+              }
+            } else {  // 4 bytes = 8 codes, low nibble first (even K)
+              const int lb = g * 32 + c * 4;
+              const uint32_t word = *reinterpret_cast<const uint32_t *>(
+                  raw + row * 128 + ((((lb >> 4) ^ (row & 7)) << 4) | (lb & 15)));
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const uint32_t b = (word >> (8 * h)) & 0xFFu;
+                const float lo = __uint_as_float(0x4B000000u | (b & 0xFu)) - zbias;
+                const float hi = __uint_as_float(0x4B000000u | (b >> 4)) - zbias;
+                packed[h] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+              }
             }
           } else {  // INT4 [K][128 features as 64 bytes]: element (k, n) -> byte k*64 + n/2
             row = idx & 127;  // feature
             c = idx >> 7;     // K chunk of 8
             const int sh = (row & 1) * 4;
-            const float bias = 8388608.0f + (float)args.w_zero_point;  // 2^23 + zp
             float vals[8];
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               const uint32_t b = raw[(c * 8 + kk) * 64 + (row >> 1)];
-              vals[kk] = __uint_as_float(0x4B000000u | ((b >> sh) & 0xFu)) - bias;
+              vals[kk] = __uint_as_float(0x4B000000u | ((b >> sh) & 0xFu)) - zbias;
             }
 #pragma unroll
             for (int h = 0; h < 4; ++h)
@@ -443,6 +528,13 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
         fence_proxy_async_smem();
+        const bool last = g == r_len - 1;
+        if (last) {
+          mbar_arrive(&rawempty[rslot]);
+          r_start = kb + 1;
+          if (r_start < k_count)
+            r_len = raw_group_len(G, r_start, k_begin, k_count, args.w_k_period);
+        }
         if (PAIR == 2)
           mbar_arrive_cluster(leader_bar(&conv[stage]));
         else
@@ -450,6 +542,10 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
+        }
+        if (last && ++rslot == R) {
+          rslot = 0;
+          rphase ^= 1;
         }
       }
     }
@@ -596,9 +692,10 @@ template <int WK>
 nk_status launch_kind(int bn, int pair, int fa, const CUtensorMap &wm, const TokenMaps &xm,
                       const TcArgs &args, int grid, cudaStream_t stream) {
   if (pair == 2) return launch_impl<WK, 256, 2, 1>(wm, xm, args, grid, stream);
-  if (fa == 2) return launch_impl<WK, 256, 1, 2>(wm, xm, args, grid, stream);
-  return bn == 256 ? launch_impl<WK, 256, 1, 1>(wm, xm, args, grid, stream)
-                   : launch_impl<WK, 64, 1, 1>(wm, xm, args, grid, stream);
+  if (WK == WK_BF16 && fa == 2) return launch_impl<WK_BF16, 256, 1, 2>(wm, xm, args, grid, stream);
+  if (bn == 256) return launch_impl<WK, 256, 1, 1>(wm, xm, args, grid, stream);
+  if (bn == 64) return launch_impl<WK, 64, 1, 1>(wm, xm, args, grid, stream);
+  return launch_impl<WK, 16, 1, 1>(wm, xm, args, grid, stream);
 }
 
 }  // namespace
@@ -612,21 +709,26 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
   if (fa == 2 && (bn != 256 || pair != 1))
     return fail(NK_UNSUPPORTED, "two accumulators need 256-token tiles on single CTAs");
   CUtensorMap wm;
-  nk_status st;
+  memset(&wm, 0, sizeof(wm));
+  nk_status st = NK_OK;
+  if (wk != WK_BF16 && fa != 1) return fail(NK_UNSUPPORTED, "quantized weights: one accumulator");
   if (wk == WK_BF16)
     st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, (uint64_t)w_k, (uint64_t)w_rows,
                   (uint64_t)ldw_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   else if (wk == WK_INT8)
     st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)w_k, (uint64_t)w_rows,
-                  (uint64_t)ldw_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+                  (uint64_t)ldw_bytes, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  else if (wk == WK_INT4NK)  // feature-major codes: rows = N, cols = K/2 bytes
+    st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)(w_k / 2), (uint64_t)w_rows,
+                  (uint64_t)ldw_bytes, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   else  // INT4 reference layout: rows = K, cols = N/2 bytes
     st = make_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)(w_rows / 2),
                   (uint64_t)w_k, (uint64_t)ldw_bytes, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != NK_OK) return st;
   TokenMaps xm;
   for (int i = 0; i < kTokenBoxes; ++i) {
-    const int box = pair == 2 ? bn / 2 : token_box_rows(i);
-    if (box > bn || (pair == 2 && i > 0)) {
+    const int box = token_box_rows(i);
+    if (box > bn / pair) {
       xm.m[i] = xm.m[0];  // unused slot
       continue;
     }
@@ -638,6 +740,7 @@ nk_status tc_gemm(int wk, const void *w, int64_t w_rows, int64_t w_k, int64_t ld
   if (grid <= 0) return ok();
   if (wk == WK_BF16) return launch_kind<WK_BF16>(bn, pair, fa, wm, xm, args, grid, stream);
   if (wk == WK_INT8) return launch_kind<WK_INT8>(bn, pair, fa, wm, xm, args, grid, stream);
+  if (wk == WK_INT4NK) return launch_kind<WK_INT4NK>(bn, pair, fa, wm, xm, args, grid, stream);
   return launch_kind<WK_INT4KN>(bn, pair, fa, wm, xm, args, grid, stream);
 }
 

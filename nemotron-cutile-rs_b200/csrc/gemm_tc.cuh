@@ -28,7 +28,12 @@
 
 namespace nk {
 
-enum WeightKind { WK_BF16 = 0, WK_INT8 = 1, WK_INT4KN = 2 };
+// WK_INT8: int8 [N,K] per-row scaled; WK_INT4KN: the reference's INT4 [K,N]
+// nibble layout; WK_INT4NK: INT4 codes feature-major [N, K/2 bytes] (element
+// (n, k) in byte n*K/2 + k/2, low nibble for even k), per-group scale/zero.
+enum WeightKind { WK_BF16 = 0, WK_INT8 = 1, WK_INT4KN = 2, WK_INT4NK = 3 };
+
+
 
 struct TcTile {  // one output tile: 128 (256 for CTA pairs) features x up to BN tokens
   int w_row;     // first weight row (feature) in the weight tensor map
@@ -58,6 +63,10 @@ struct TcArgs {
   const float *tok_scale;   // [activation rows] per token (routing weight) or null
   int relu2;
   int w_zero_point;         // INT4 zero point
+  // per-group (expert) INT4 parameters: group g = weight row / group_rows
+  const float *group_scale; // [groups] or null
+  const uint8_t *group_zp;  // [groups] or null (w_zero_point then)
+  int group_rows;
   int *err;
 };
 
@@ -65,16 +74,25 @@ struct TcArgs {
 // (boxes above the tile's BN unused): each stage loads the token rows with
 // ONE TMA copy of the smallest box that covers the rows the MMA reads, so a
 // decode tile of a few tokens, or an expert's 192 routed rows, does not move
-// a full BN-row tile.  CTA pairs use m[0] only (a BN/2-row box per CTA).
+// a full BN-row tile.  In CTA pairs each CTA loads its half of the MMA's rows
+// with the smallest box (up to BN/2 rows) covering them.
 constexpr int kTokenBoxes = 9;
 __host__ __device__ constexpr int token_box_rows(int i) { return i < 2 ? 16 << i : 32 * i; }
 struct TokenMaps {
   CUtensorMap m[kTokenBoxes];
 };
 
+// Raw (quantized) weight tile as TMA delivers it.  Feature-major kinds load
+// 128 bytes of every weight row at once (whole 128-byte lines): kGroup K
+// blocks per raw tile, int8 [128 rows x 2 K blocks of 64 B], INT4 [128 rows x
+// 4 K blocks of 32 B]; the reference INT4 [K,N] layout [64 K rows x 64 B
+// (128 features)] one K block per tile.
 template <int WK>
 struct WeightTile {
-  static constexpr int kRawBytes = WK == WK_BF16 ? 0 : (WK == WK_INT8 ? 128 * 64 : 64 * 64);
+  static constexpr int kGroup = WK == WK_INT8 ? 2 : (WK == WK_INT4NK ? 4 : 1);
+  static constexpr int kRowBytes = WK == WK_INT8 ? 64 : (WK == WK_INT4NK ? 32 : 64);
+  static constexpr int kRawBytes =
+      WK == WK_BF16 ? 0 : (WK == WK_INT4KN ? 64 * 64 : 128 * 128);
 };
 
 // PAIR = 1: one CTA computes 128·FA features x BN tokens.
@@ -86,28 +104,38 @@ struct WeightTile {
 // double-buffered ones); the token bytes per weight byte halve.
 template <int WK, int BN, int PAIR = 1, int FA = 1>
 struct TcConfig {
-  static_assert(FA == 1 || (FA == 2 && PAIR == 1), "two accumulators only for single CTAs");
+  static_assert(FA == 1 || (FA == 2 && PAIR == 1 && WK == WK_BF16),
+                "two accumulators only for single CTAs with bf16 weights");
+  static constexpr bool kQuant = WK != WK_BF16;
   static constexpr int kATileBytes = 128 * 128;     // 128 weight rows x 64 bf16
   static constexpr int kABytes = kATileBytes * FA;
   static constexpr int kBRows = BN / PAIR;          // token rows loaded per CTA
   static constexpr int kBBytes = kBRows * 128;      // kBRows x 64 bf16
-  static constexpr int kRawTileBytes = WeightTile<WK>::kRawBytes;
-  static constexpr int kRawBytes = kRawTileBytes * FA;
-  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
-  static constexpr int kStages0 = (224 * 1024) / kStageBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
 #ifndef NK_STAGES_MAX
-#define NK_STAGES_MAX 8
+#define NK_STAGES_MAX 16
 #endif
+  // Quantized kinds: a main ring of 3-4 stages (bf16 weight tile + token
+  // tile) and a separate, deeper ring of raw tiles that the producer fills
+  // ahead of it, so conversion never waits on a load.
+  static constexpr int kRawTileBytes = WeightTile<WK>::kRawBytes;
+  static constexpr int kStages0 =
+      kQuant ? (224 * 1024 - (BN <= 64 ? 6 : 4) * kRawTileBytes) / kStageBytes
+             : (224 * 1024) / kStageBytes;
   static constexpr int kStages = kStages0 > NK_STAGES_MAX ? NK_STAGES_MAX : kStages0;
+  static constexpr int kRawSlots0 =
+      kQuant ? (224 * 1024 - kStages * kStageBytes) / kRawTileBytes : 0;
+  static constexpr int kRawSlots = kRawSlots0 > 16 ? 16 : kRawSlots0;
 #ifndef NK_TRANSFORM_THREADS
 #define NK_TRANSFORM_THREADS 256
 #endif
-  static constexpr int kTransformThreads = WK == WK_BF16 ? 0 : NK_TRANSFORM_THREADS * FA;
+  static constexpr int kTransformThreads = kQuant ? NK_TRANSFORM_THREADS : 0;
   static constexpr int kEpiThreads = 128 * FA;      // 4 warps per accumulator
   static constexpr int kThreads = 64 + kEpiThreads + kTransformThreads;
   static constexpr int kAccSlots = 2 / FA;          // accumulator sets in TMEM
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
+  static constexpr int kSmemBytes =
+      1024 + kStages * kStageBytes + kRawSlots * kRawTileBytes + 768;
   static constexpr int kFeatRows = 128 * PAIR * FA; // features per output tile
 };
 

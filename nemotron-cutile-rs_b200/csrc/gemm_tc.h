@@ -8,7 +8,7 @@ namespace nk {
 // w_rows feature rows of w_k elements, row pitch ldw_bytes; or WK_INT4KN with
 // the reference [K,N] nibble layout (w_rows = N features, w_k = K rows,
 // ldw_bytes = N/2).  Activations (B): bf16 [x_rows, x_k], pitch ldx_elems.
-// bn: 256 or 64 token rows per tile.  grid: CTAs (persistent over tiles).
+// bn: 256, 64 or 16 token rows per tile.  grid: CTAs (persistent over tiles).
 // pair = 2: clusters of two CTAs share 256-feature tiles (tcgen05 cta_group::2);
 // needs bn = 256, an even grid, and tiles of 256 features (f_tiles / tile lists
 // built with 256-row feature tiles).

@@ -6,6 +6,7 @@
 //   -> shared expert (two dense GEMMs) -> rank-ordered combine.
 #include <stdlib.h>
 
+#include "ep.h"
 #include "gemm_tc.h"
 #include "route.h"
 
@@ -265,6 +266,17 @@ MoeWorkspace carve(const nk_moe_layer &L, int64_t T, uint8_t *base) {
   return ws;
 }
 
+// INT4 rows of K codes are K/2 bytes, loaded by TMA in 16-byte steps.
+nk_status validate_weight_kind(const nk_moe_layer *L) {
+  if (L->weight_kind != NK_W_BF16 && L->weight_kind != NK_W_INT8_ROW &&
+      L->weight_kind != NK_W_INT4_AFFINE)
+    return fail(NK_UNSUPPORTED, "weight_kind");
+  if (L->weight_kind == NK_W_INT4_AFFINE &&
+      (L->hidden % 32 || L->inter % 32 || L->shared_inter % 32))
+    return fail(NK_UNSUPPORTED, "INT4_AFFINE experts need hidden, inter, shared_inter % 32 == 0");
+  return NK_OK;
+}
+
 nk_status validate(const nk_moe_layer *L) {
   if (!L) return fail(NK_INVALID_SHAPE, "null layer");
   if (L->hidden <= 0 || L->experts <= 0 || L->top_k <= 0 || L->top_k > L->experts ||
@@ -274,18 +286,23 @@ nk_status validate(const nk_moe_layer *L) {
     return fail(NK_UNSUPPORTED, "experts <= 1024 and top_k <= 32");
   if (L->hidden % 8 || L->inter % 16 || (L->shared_inter % 16))
     return fail(NK_UNSUPPORTED, "hidden % 8 == 0 and inter, shared_inter % 16 == 0 required");
-  if (L->weight_kind != NK_W_BF16 && L->weight_kind != NK_W_INT8_ROW)
-    return fail(NK_UNSUPPORTED, "weight_kind");
+  nk_status st = validate_weight_kind(L);
+  if (st != NK_OK) return st;
   if (L->route_mode < NK_ROUTE_SIGMOID || L->route_mode > NK_ROUTE_SIGMOID_RENORM)
     return fail(NK_UNSUPPORTED, "route_mode");
   if (!L->router_w3 || !L->up_w || !L->down_w) return fail(NK_INVALID_PARAMS, "missing weights");
-  if (L->weight_kind == NK_W_INT8_ROW && (!L->up_scale || !L->down_scale))
-    return fail(NK_INVALID_PARAMS, "INT8_ROW weights need scales");
+  if (L->weight_kind != NK_W_BF16 && (!L->up_scale || !L->down_scale))
+    return fail(NK_INVALID_PARAMS, "quantized expert weights need scales");
+  if (L->weight_kind == NK_W_INT4_AFFINE && (!L->up_zero_point || !L->down_zero_point))
+    return fail(NK_INVALID_PARAMS, "INT4_AFFINE expert weights need zero points");
   if (L->shared_inter > 0 && (!L->shared_up_w || !L->shared_down_w))
     return fail(NK_INVALID_PARAMS, "missing shared expert weights");
-  if (L->shared_inter > 0 && L->weight_kind == NK_W_INT8_ROW &&
+  if (L->shared_inter > 0 && L->weight_kind != NK_W_BF16 &&
       (!L->shared_up_scale || !L->shared_down_scale))
-    return fail(NK_INVALID_PARAMS, "INT8_ROW shared expert needs scales");
+    return fail(NK_INVALID_PARAMS, "quantized shared expert needs scales");
+  if (L->shared_inter > 0 && L->weight_kind == NK_W_INT4_AFFINE &&
+      (!L->shared_up_zero_point || !L->shared_down_zero_point))
+    return fail(NK_INVALID_PARAMS, "INT4_AFFINE shared expert needs zero points");
   return NK_OK;
 }
 
@@ -296,12 +313,37 @@ nk_status validate_experts(const nk_moe_layer *L) {
     return fail(NK_INVALID_SHAPE, "hidden, experts and inter must be positive");
   if (L->hidden % 8 || L->inter % 16)
     return fail(NK_UNSUPPORTED, "hidden % 8 == 0 and inter % 16 == 0 required");
-  if (L->weight_kind != NK_W_BF16 && L->weight_kind != NK_W_INT8_ROW)
-    return fail(NK_UNSUPPORTED, "weight_kind");
+  nk_status st = validate_weight_kind(L);
+  if (st != NK_OK) return st;
   if (!L->up_w || !L->down_w) return fail(NK_INVALID_PARAMS, "missing expert weights");
-  if (L->weight_kind == NK_W_INT8_ROW && (!L->up_scale || !L->down_scale))
-    return fail(NK_INVALID_PARAMS, "INT8_ROW weights need scales");
+  if (L->weight_kind != NK_W_BF16 && (!L->up_scale || !L->down_scale))
+    return fail(NK_INVALID_PARAMS, "quantized expert weights need scales");
+  if (L->weight_kind == NK_W_INT4_AFFINE && (!L->up_zero_point || !L->down_zero_point))
+    return fail(NK_INVALID_PARAMS, "INT4_AFFINE expert weights need zero points");
   return NK_OK;
+}
+
+// One GEMM's weight operand in the layer's kind: tc_gemm kind, row pitch for
+// K inputs, and the epilogue / transform parameters (per-row int8 scales, or
+// per-expert INT4 scale and zero point for groups of `rows` weight rows).
+struct WOp {
+  int wk;
+  const void *w;
+  const float *scale;
+  const uint8_t *zp;
+};
+int moe_wk(const nk_moe_layer &L) {
+  return L.weight_kind == NK_W_INT8_ROW ? WK_INT8
+                                        : (L.weight_kind == NK_W_INT4_AFFINE ? WK_INT4NK : WK_BF16);
+}
+int64_t w_pitch(int wk, int64_t k) { return wk == WK_BF16 ? 2 * k : (wk == WK_INT8 ? k : k / 2); }
+void apply_wop(TcArgs &a, const WOp &op, int group_rows) {
+  if (op.wk == WK_INT8) a.row_scale = op.scale;
+  if (op.wk == WK_INT4NK) {
+    a.group_scale = op.scale;
+    a.group_zp = op.zp;
+    a.group_rows = group_rows;
+  }
 }
 
 TcArgs base_args(int *err) {
@@ -322,10 +364,20 @@ int grouped_fa() {
   return v;
 }
 
-nk_status dense(int wk, const void *w, const float *row_scale, const float *bias,
-                const uint16_t *x, int64_t T, int64_t k, int64_t n_out, void *y, bool y_f32,
-                bool relu2, int *err, cudaStream_t s, int max_ctas = 0) {
-  const int bn = T <= 64 ? 64 : 256;
+// CTA pairs for the grouped GEMMs: NK_GROUPED_PAIR=2 selects them (default
+// single CTAs).
+int grouped_pair() {
+  static const int v = [] {
+    const char *e = getenv("NK_GROUPED_PAIR");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
+nk_status dense(const WOp &op, const float *bias, const uint16_t *x, int64_t T, int64_t k,
+                int64_t n_out, void *y, bool y_f32, bool relu2, int *err, cudaStream_t s,
+                int max_ctas = 0) {
+  const int bn = T <= 16 ? 16 : (T <= 64 ? 64 : 256);
   TcArgs a = base_args(err);
   a.f_tiles = (int)ceil_div(n_out, 128);
   a.t_tiles = (int)ceil_div(T, bn);
@@ -335,13 +387,13 @@ nk_status dense(int wk, const void *w, const float *row_scale, const float *bias
   a.y = y;
   a.ldy = n_out;
   a.y_f32 = y_f32;
-  a.row_scale = row_scale;
+  apply_wop(a, op, (int)n_out);
   a.bias = bias;
   a.relu2 = relu2;
   int64_t tiles = (int64_t)a.f_tiles * a.t_tiles;
   const int ctas = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
   int grid = (int)(tiles < ctas ? tiles : ctas);
-  return tc_gemm(wk, w, n_out, k, wk == WK_BF16 ? 2 * k : k, x, T, k, k, bn, a, grid, s);
+  return tc_gemm(op.wk, op.w, n_out, k, w_pitch(op.wk, k), x, T, k, k, bn, a, grid, s);
 }
 
 }  // namespace
@@ -364,7 +416,7 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
   int router_splits = 1;
   {
     const int64_t hp = ceil_div(H, 64) * 64;
-    const int bn = T <= 64 ? 64 : 256;
+    const int bn = T <= 16 ? 16 : (T <= 64 ? 64 : 256);
     const int k_blocks = (int)(2 * hp / 64);  // hi and mid parts; lo enters the bound
     TcArgs a = base_args(err);
     a.f_tiles = (int)ceil_div(E, 128);
@@ -418,10 +470,15 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   const int ctas = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
   int *err = device_error_ptr();
   const int64_t E = L.experts, H = L.hidden, I = L.inter;
-  const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
-  // bf16 experts: 256-feature tiles with two accumulators per CTA (each
-  // token tile is loaded once per 256 features instead of once per 128)
-  const int fa = wk == WK_BF16 ? grouped_fa() : 1;
+  const int wk = moe_wk(L);
+  // bf16 experts: 256-feature tiles on single CTAs with two accumulators, so
+  // each token tile is loaded once per 256 features.  Quantized experts: one
+  // accumulator (their transform warps need the registers).  CTA pairs
+  // (NK_GROUPED_PAIR=2) measured 1.5-2.5x slower here.
+  const int gp = grouped_pair();
+  const int pair = gp == 2 ? 2 : 1;
+  const int fa = wk == WK_BF16 && pair == 1 ? grouped_fa() : 1;
+  const int gctas = pair == 2 ? (ctas & ~1) : ctas;
   TileLists lists;
   lists.n_out[0] = (int)I;
   lists.n_out[1] = (int)H;
@@ -429,7 +486,8 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   lists.tiles[1] = ws.tiles_down;
   lists.count[0] = ws.tile_counts;
   lists.count[1] = ws.tile_counts + 1;
-  build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, 128 * fa, lists);
+  build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, 128 * fa * pair,
+                                        lists);
   nk_status st = check_launch("build_tiles_kernel");
   if (st != NK_OK) return st;
   if (R == 0) return NK_OK;
@@ -441,11 +499,11 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
     a.k_blocks = (int)ceil_div(H, 64);
     a.y = ws.hmid;
     a.ldy = I;
-    a.row_scale = wk == WK_INT8 ? L.up_scale : nullptr;
+    apply_wop(a, WOp{wk, L.up_w, L.up_scale, L.up_zero_point}, (int)I);
     a.bias = L.up_b;
     a.relu2 = 1;
-    st = tc_gemm(wk, L.up_w, E * I, H, wk == WK_BF16 ? 2 * H : H, rows, R, H, H, kMoeBN, a,
-                 ctas, s, 1, fa);
+    st = tc_gemm(wk, L.up_w, E * I, H, w_pitch(wk, H), rows, R, H, H, kMoeBN, a, gctas, s, pair,
+                 fa);
     if (st != NK_OK) return st;
   }
   tm.mark(4, s);
@@ -456,10 +514,10 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
     a.k_blocks = (int)ceil_div(I, 64);
     a.y = out;
     a.ldy = H;
-    a.row_scale = wk == WK_INT8 ? L.down_scale : nullptr;
+    apply_wop(a, WOp{wk, L.down_w, L.down_scale, L.down_zero_point}, (int)H);
     a.bias = L.down_b;
-    st = tc_gemm(wk, L.down_w, E * H, I, wk == WK_BF16 ? 2 * I : I, ws.hmid, R, I, I, kMoeBN, a,
-                 ctas, s, 1, fa);
+    st = tc_gemm(wk, L.down_w, E * H, I, w_pitch(wk, I), ws.hmid, R, I, I, kMoeBN, a, gctas, s,
+                 pair, fa);
   }
   return st;
 }
@@ -467,12 +525,12 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
 nk_status shared_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, uint16_t *s1,
                        uint16_t *sh, cudaStream_t s, int max_ctas = 0) {
   int *err = device_error_ptr();
-  const int wk = L.weight_kind == NK_W_INT8_ROW ? WK_INT8 : WK_BF16;
+  const int wk = moe_wk(L);
   const int64_t Is = L.shared_inter, H = L.hidden;
-  nk_status st = dense(wk, L.shared_up_w, wk == WK_INT8 ? L.shared_up_scale : nullptr,
+  nk_status st = dense(WOp{wk, L.shared_up_w, L.shared_up_scale, L.shared_up_zero_point},
                        L.shared_up_b, x, T, H, Is, s1, false, true, err, s, max_ctas);
   if (st != NK_OK) return st;
-  return dense(wk, L.shared_down_w, wk == WK_INT8 ? L.shared_down_scale : nullptr,
+  return dense(WOp{wk, L.shared_down_w, L.shared_down_scale, L.shared_down_zero_point},
                L.shared_down_b, s1, T, Is, H, sh, false, false, err, s, max_ctas);
 }
 
@@ -582,6 +640,117 @@ nk_status moe_forward(const nk_moe_layer &L, const uint16_t *x, int64_t T, void 
   }
   tm.mark(6, s);
   st = combine_stage(ws.xp, ws.sh, rw, ws.slot_pos, T, L.hidden, (int)K, out, out_dtype, s);
+  tm.mark(7, s);
+  return st;
+}
+
+// Scratch of nk_moe_forward_ep.
+struct EpWorkspace {
+  DispatchWs d;
+  ExpertsWs x;
+  int32_t *idx, *counts, *offsets, *slot_pos;
+  float *w;
+  uint16_t *s1, *sh;
+  size_t bytes;
+};
+
+EpWorkspace carve_ep(const nk_moe_layer &L, const nk_moe_layer &local, const nk_ep_ctx &c,
+                     int64_t T, uint8_t *base) {
+  EpWorkspace ws{};
+  Carver cv{base};
+  const int64_t E = L.experts, S = T * L.top_k;
+  ws.d = carve_dispatch(L, T, cv);
+  ws.x = carve_experts(local, c.capacity_rows, (int64_t)c.ranks * local.experts, cv);
+  ws.idx = (int32_t *)cv.take(sizeof(int32_t) * S);
+  ws.w = (float *)cv.take(sizeof(float) * S);
+  ws.counts = (int32_t *)cv.take(sizeof(int32_t) * E);
+  ws.offsets = (int32_t *)cv.take(sizeof(int32_t) * (E + 1));
+  ws.slot_pos = (int32_t *)cv.take(sizeof(int32_t) * S);
+  if (L.shared_inter > 0) {
+    ws.s1 = (uint16_t *)cv.take(2 * T * L.shared_inter);
+    ws.sh = (uint16_t *)cv.take(2 * T * L.hidden);
+  }
+  ws.bytes = cv.off;
+  return ws;
+}
+
+nk_status validate_ep(const nk_ep_ctx *c, const nk_moe_layer *L, const nk_moe_layer *local,
+                      int64_t T) {
+  if (!c || !c->connected) return fail(NK_INVALID_PARAMS, "connected nk_ep_ctx required");
+  nk_status st = validate(L);
+  if (st != NK_OK) return st;
+  st = validate_experts(local);
+  if (st != NK_OK) return st;
+  if (L->experts != c->experts || L->hidden != c->hidden || L->top_k != c->top_k ||
+      local->experts * c->ranks != c->experts || local->hidden != c->hidden ||
+      local->inter != L->inter || local->weight_kind != L->weight_kind)
+    return fail(NK_INVALID_SHAPE, "layer, local experts and context disagree");
+  if (T <= 0) return fail(NK_INVALID_ROW_COUNT, "row_count must be non-zero");
+  if (T > c->max_tokens) return fail(NK_INVALID_SHAPE, "more tokens than the context holds");
+  return NK_OK;
+}
+
+// MoeLayer::forward_into (moe.rs:154-249) with the experts spread over ranks:
+// route here, exchange counts, send each routed row straight into its
+// expert owner's receive buffer, run this rank's experts on what arrived,
+// send the results straight back, combine in rank order.  Device barriers in
+// peer memory order the phases; no host synchronisation, no collectives.
+nk_status moe_forward_ep(nk_ep_ctx *c, const nk_moe_layer &L, const nk_moe_layer &local,
+                         const uint16_t *x, int64_t T, void *out, int out_dtype,
+                         int32_t *indices, float *weights, void *workspace, size_t ws_bytes,
+                         cudaStream_t s) {
+  const EpWorkspace need = carve_ep(L, local, *c, T, nullptr);
+  if (!workspace || ws_bytes < need.bytes) return ws_too_small(need.bytes, ws_bytes);
+  EpWorkspace ws = carve_ep(L, local, *c, T, reinterpret_cast<uint8_t *>(workspace));
+  int32_t *idx = indices ? indices : ws.idx;
+  float *rw = weights ? weights : ws.w;
+  StageTimer &tm = timer();
+  tm.recorded = false;
+  nk_status st;
+  // shared expert beside the exchange (side stream, a share of the SMs)
+  const int sh_sms = L.shared_inter > 0 ? shared_expert_sms(L, T) : 0;
+  const bool overlap = sh_sms > 0 && sh_sms < num_sms();
+  SideStream *side = nullptr;
+  if (overlap) {
+    st = side_stream(&side);
+    if (st != NK_OK) return st;
+    NK_CUDA_TRY(cudaEventRecord(side->fork, s));
+    NK_CUDA_TRY(cudaStreamWaitEvent(side->stream, side->fork, 0));
+    st = shared_stage(L, x, T, ws.s1, ws.sh, side->stream, sh_sms);
+    if (st != NK_OK) return st;
+    NK_CUDA_TRY(cudaEventRecord(side->join, side->stream));
+  }
+  st = dispatch_stage(L, x, T, idx, rw, ws.counts, ws.offsets, ws.slot_pos, nullptr, ws.d, tm, s);
+  if (st != NK_OK) return st;
+  st = ep_exchange_counts(c, ws.counts, s);  // also: every peer is done with the last forward
+  if (st != NK_OK) return st;
+  st = ep_plan(c, s);
+  if (st != NK_OK) return st;
+  st = ep_dispatch(c, x, T, idx, ws.slot_pos, ws.offsets, s);
+  if (st != NK_OK) return st;
+  st = ep_barrier(c, s);  // every routed row has arrived
+  if (st != NK_OK) return st;
+  uint16_t *recv = ep_recv(c);
+  st = experts_stage(local, recv, c->capacity_rows, c->seg_expert, c->seg_rows,
+                     c->ranks * (int)local.experts, recv, ws.x, tm, s,
+                     overlap ? num_sms() - sh_sms : 0);
+  if (st != NK_OK) return st;
+  st = ep_return(c, s);
+  if (st != NK_OK) return st;
+  st = ep_barrier(c, s);  // every result is back
+  if (st != NK_OK) return st;
+  tm.mark(5, s);
+  if (L.shared_inter > 0) {
+    if (overlap) {
+      NK_CUDA_TRY(cudaStreamWaitEvent(s, side->join, 0));
+    } else {
+      st = shared_stage(L, x, T, ws.s1, ws.sh, s);
+      if (st != NK_OK) return st;
+    }
+  }
+  tm.mark(6, s);
+  st = combine_stage(ep_out(c), ws.sh, rw, ws.slot_pos, T, L.hidden, (int)L.top_k, out,
+                     out_dtype, s);
   tm.mark(7, s);
   return st;
 }
@@ -708,6 +877,29 @@ nk_status nk_moe_stage_times(float *ms, int32_t capacity, int32_t *count) {
   for (int i = 0; i < n; ++i) NK_CUDA_TRY(cudaEventElapsedTime(&ms[i], t.ev[i], t.ev[i + 1]));
   if (count) *count = n;
   return ok();
+}
+
+
+nk_status nk_moe_forward_ep_workspace_bytes(const nk_ep_ctx *ctx, const nk_moe_layer *layer,
+                                            const nk_moe_layer *local, int64_t tokens,
+                                            size_t *bytes) {
+  nk_status st = validate_ep(ctx, layer, local, tokens);
+  if (st != NK_OK) return st;
+  if (!bytes) return fail(NK_INVALID_PARAMS, "bytes is null");
+  *bytes = carve_ep(*layer, *local, *ctx, tokens, nullptr).bytes;
+  return ok();
+}
+
+nk_status nk_moe_forward_ep(nk_ep_ctx *ctx, const nk_moe_layer *layer, const nk_moe_layer *local,
+                            const uint16_t *x, int64_t tokens, void *out, int32_t out_dtype,
+                            int32_t *indices, float *weights, void *workspace,
+                            size_t workspace_bytes, void *stream) {
+  nk_status st = validate_ep(ctx, layer, local, tokens);
+  if (st != NK_OK) return st;
+  if (out_dtype != NK_F32 && out_dtype != NK_BF16) return fail(NK_UNSUPPORTED, "out_dtype");
+  st = moe_forward_ep(ctx, *layer, *local, x, tokens, out, out_dtype, indices, weights,
+                      workspace, workspace_bytes, as_stream(stream));
+  return st == NK_OK ? ok() : st;
 }
 
 }  // extern "C"

@@ -65,6 +65,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int *er
   }
 }
 
+// Bounded wait for roles that are not on the issue-critical path (epilogue,
+// transform): after a few polls it sleeps between polls, so waiting warps do
+// not take issue slots from the single-thread producer and MMA warps.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t phase, int *err) {
+  for (int i = 0; i < 4; ++i)
+    if (mbar_try_wait(bar, phase)) return true;
+  uint64_t t0 = nk_globaltimer();
+  uint32_t ns = 32;
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((it & 15u) == 0) {
+      if (nk_globaltimer() - t0 > NK_WAIT_LIMIT_NS) {
+        atomicCAS(err, 0, NK_TIMEOUT);
+        return false;
+      }
+      if (*(volatile int *)err != 0) return false;  // another role already gave up
+    }
+  }
+}
+
 // ----------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -79,6 +101,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// 16-byte global load through the read-only path, not kept in L1 (weights
+// are read once per tile).
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (tensor core).

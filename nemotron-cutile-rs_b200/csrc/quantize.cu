@@ -116,6 +116,24 @@ __global__ void router_split_kernel(const float *__restrict__ w, int64_t E, int6
   row[2 * Hp + h] = lo;
 }
 
+// INT4 codes in the reference's [K,N] nibble layout (flat index k*N + n in
+// byte index/2, low nibble for even index) -> feature-major [N, K/2] bytes
+// (byte n*K/2 + k/2, low nibble for even k), `batch` matrices back to back.
+__global__ void int4_kn_to_nk_kernel(const uint8_t *__restrict__ kn, int64_t batch, int64_t K,
+                                     int64_t N, uint8_t *__restrict__ nk) {
+  const int64_t per = N * (K / 2);
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= batch * per) return;
+  const int64_t b = idx / per, r = idx - b * per;
+  const int64_t n = r / (K / 2), kk = (r - n * (K / 2)) * 2;
+  const uint8_t *src = kn + b * ((K * N + 1) / 2);
+  auto code = [&](int64_t k) -> uint32_t {
+    const int64_t f = k * N + n;
+    return (src[f >> 1] >> ((f & 1) * 4)) & 0xFu;
+  };
+  nk[idx] = (uint8_t)(code(kk) | (code(kk + 1) << 4));
+}
+
 // f32 [K,N] -> bf16 [N,K] (32x32 tiles through shared memory).
 __global__ void pack_kn_kernel(const float *__restrict__ src, int64_t K, int64_t N,
                                __nv_bfloat16 *__restrict__ dst) {
@@ -284,6 +302,16 @@ nk_status nk_router_split(const float *router_w, int64_t experts, int64_t hidden
   router_split_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, as_stream(stream)>>>(
       router_w, experts, hidden, hp, reinterpret_cast<__nv_bfloat16 *>(router_w3));
   return check_launch("router_split_kernel");
+}
+
+nk_status nk_int4_kn_to_nk(const uint8_t *packed_kn, int64_t batch, int64_t k, int64_t n,
+                           uint8_t *packed_nk, void *stream) {
+  if (batch <= 0 || k <= 0 || n <= 0) return fail(NK_INVALID_SHAPE, "batch, k and n must be positive");
+  if (k % 2) return fail(NK_UNSUPPORTED, "k must be even");
+  const int64_t total = batch * n * (k / 2);
+  int4_kn_to_nk_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, as_stream(stream)>>>(
+      packed_kn, batch, k, n, packed_nk);
+  return check_launch("int4_kn_to_nk_kernel");
 }
 
 nk_status nk_linear_pack_kn(const float *w_kn, int64_t k, int64_t n, uint16_t *w_nk,

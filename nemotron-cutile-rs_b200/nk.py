@@ -66,6 +66,8 @@ class NkMoeLayer(_c.Structure):
         ("down_w", _p), ("down_scale", _p), ("down_b", _p),
         ("shared_up_w", _p), ("shared_up_scale", _p), ("shared_up_b", _p),
         ("shared_down_w", _p), ("shared_down_scale", _p), ("shared_down_b", _p),
+        ("up_zero_point", _p), ("down_zero_point", _p),
+        ("shared_up_zero_point", _p), ("shared_down_zero_point", _p),
     ]
 
 
@@ -126,9 +128,18 @@ _SIGS = {
     "nk_gemm_w4a_ws": (_i32, [_p, _i32, _p, _sz, _f, _u32, _p, _p, _i32, _i64, _i64, _i64, _i32,
                               _p, _sz, _p]),
     "nk_scratch_release": (_i32, [_p]),
+    "nk_ep_handle_bytes": (_sz, []),
+    "nk_ep_create": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p]),
+    "nk_ep_connect": (_i32, [_p, _p]),
+    "nk_moe_forward_ep_workspace_bytes": (_i32, [_p, _p, _p, _i64, _p]),
+    "nk_moe_forward_ep": (_i32, [_p, _p, _p, _p, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+    "nk_ep_barrier": (_i32, [_p, _p]),
+    "nk_ep_received_rows": (_i32, [_p, _p]),
+    "nk_ep_destroy": (_i32, [_p]),
     "nk_pack_int4": (_i32, [_p, _sz, _p, _sz, _p]),
     "nk_unpack_int4": (_i32, [_p, _sz, _sz, _p, _sz, _p]),
     "nk_quantize_int4": (_i32, [_p, _sz, _f, _u32, _p, _sz, _p]),
+    "nk_int4_kn_to_nk": (_i32, [_p, _i64, _i64, _i64, _p, _p]),
     "nk_dequantize_int4": (_i32, [_p, _sz, _sz, _f, _u32, _p, _sz, _p]),
     "nk_validate_int4_params": (_i32, [_f, _u32]),
     "nk_quantize_int8_row": (_i32, [_p, _i64, _i64, _p, _p, _p]),
@@ -369,6 +380,32 @@ def quantize_int8_row(w, stream=None):
     return q, s
 
 
+def quantize_int4_experts(w, zero_point: int = 8, stream=None):
+    """Expert weights w [E, N, K] (output-major, any float dtype) in the
+    reference's INT4-affine format, one per-tensor (scale, zero_point) per
+    expert: scale = max|W_e| / 7 as the benchmark configurations state, codes
+    from nk_quantize_int4 (quantize.rs:131-144) on W_eᵀ in the reference's
+    [K, N] = [input_dim, output_dim] layout.  Returns (codes [E, N, K/2] uint8
+    feature-major for NK_W_INT4_AFFINE, scales f32 [E], zero points uint8 [E],
+    reference packed bytes [E, ceil(K*N/2)])."""
+    import torch
+
+    e, n, k = w.shape
+    wf = w.float()
+    scales = (wf.abs().amax(dim=(1, 2)) / 7.0).to(torch.float32)
+    kn_len = (k * n + 1) // 2
+    packed = torch.empty((e, kn_len), dtype=torch.uint8, device=w.device)
+    sc = scales.cpu().tolist()
+    for i in range(e):
+        t = wf[i].t().contiguous()  # [K, N]
+        call("nk_quantize_int4", ptr(t), k * n, float(sc[i]), zero_point, ptr(packed[i]), kn_len,
+             stream_ptr(stream))
+    codes = torch.empty((e, n, k // 2), dtype=torch.uint8, device=w.device)
+    call("nk_int4_kn_to_nk", ptr(packed), e, k, n, ptr(codes), stream_ptr(stream))
+    zps = torch.full((e,), zero_point, dtype=torch.uint8, device=w.device)
+    return codes, scales, zps, packed
+
+
 def router_split(w, stream=None):
     import torch
 
@@ -403,6 +440,10 @@ class MoeWeights:
     shared_down_w: object = None
     shared_down_scale: object = None
     shared_down_b: object = None
+    up_zero_point: object = None          # INT4_AFFINE: uint8 [E]
+    down_zero_point: object = None
+    shared_up_zero_point: object = None   # uint8 [1]
+    shared_down_zero_point: object = None
 
     def struct(self) -> NkMoeLayer:
         s = NkMoeLayer()
@@ -411,7 +452,8 @@ class MoeWeights:
             setattr(s, f, getattr(self, f))
         for f in ("router_w3", "router_b", "up_w", "up_scale", "up_b", "down_w", "down_scale",
                   "down_b", "shared_up_w", "shared_up_scale", "shared_up_b", "shared_down_w",
-                  "shared_down_scale", "shared_down_b"):
+                  "shared_down_scale", "shared_down_b", "up_zero_point", "down_zero_point",
+                  "shared_up_zero_point", "shared_down_zero_point"):
             setattr(s, f, ptr(getattr(self, f)))
         return s
 

@@ -326,6 +326,105 @@ class PeerExpertParallelMoe:
         self._opened, self._owned = [], []
 
 
+class NativeExpertParallelMoe:
+    """Expert parallelism behind the C ABI (nk_ep_create / nk_ep_connect /
+    nk_moe_forward_ep): the whole layer runs inside libnk on this rank's
+    stream — routing, the counts exchange, the row exchange over NVLink peer
+    stores, the grouped experts, the return and the combine, ordered by device
+    barriers in peer memory.  torch.distributed is used once, to gather the
+    ranks' handle blobs at construction (what a Rust host does with its own
+    collective).
+
+    full: the whole layer (router over all experts, shared expert); local:
+    this rank's experts (nk.MoeWeights with experts = E / G)."""
+
+    def __init__(self, full: nk.MoeWeights, local: nk.MoeWeights, max_tokens: int, group=None,
+                 capacity_rows: int = 0):
+        import ctypes as C
+
+        self.full, self.local, self.group = full, local, group
+        self.G = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        self.T_max = max_tokens
+        self._fs, self._ls = full.struct(), local.struct()
+        nbytes = nk.lib().nk_ep_handle_bytes()
+        blob = (C.c_uint8 * nbytes)()
+        ctx = C.c_void_p()
+        nk.call("nk_ep_create", self.G, self.me, full.experts, full.hidden, full.top_k,
+                max_tokens, capacity_rows, C.byref(ctx), blob)
+        self.ctx = ctx
+        dev = torch.device("cuda", torch.cuda.current_device())
+        mine = torch.tensor(list(bytes(blob)), dtype=torch.uint8, device=dev)
+        allb = torch.empty(self.G * nbytes, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(allb, mine, group=group)
+        allb = (C.c_uint8 * (self.G * nbytes))(*allb.cpu().tolist())
+        nk.call("nk_ep_connect", self.ctx, allb)
+        self._ws = None
+        self.rows = torch.zeros(1, dtype=torch.int32, device=dev)
+        dist.barrier(group=group)
+
+    def forward(self, x, out=None, out_dtype=torch.float32, indices=None, weights=None):
+        import ctypes as C
+
+        t = x.shape[0]
+        need = C.c_size_t()
+        nk.call("nk_moe_forward_ep_workspace_bytes", self.ctx, C.byref(self._fs),
+                C.byref(self._ls), t, C.byref(need))
+        if self._ws is None or self._ws.numel() < need.value:
+            self._ws = torch.empty(need.value, dtype=torch.uint8, device=x.device)
+        k = self.full.top_k
+        idx = indices if indices is not None else torch.empty(t * k, dtype=torch.int32,
+                                                              device=x.device)
+        w = weights if weights is not None else torch.empty(t * k, dtype=torch.float32,
+                                                            device=x.device)
+        if out is None:
+            out = torch.empty(t, self.full.hidden, dtype=out_dtype, device=x.device)
+        od = nk.F32 if out.dtype == torch.float32 else nk.BF16
+        nk.call("nk_moe_forward_ep", self.ctx, C.byref(self._fs), C.byref(self._ls), nk.ptr(x),
+                t, nk.ptr(out), od, nk.ptr(idx), nk.ptr(w), nk.ptr(self._ws), self._ws.numel(),
+                nk.stream_ptr())
+        return out, idx, w
+
+    def received_rows(self) -> int:
+        torch.cuda.synchronize()
+        nk.call("nk_ep_received_rows", self.ctx, nk.ptr(self.rows))
+        torch.cuda.synchronize()
+        return int(self.rows.item())
+
+    def close(self):
+        if self.ctx is None:
+            return
+        nk.call("nk_ep_barrier", self.ctx, nk.stream_ptr())
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        nk.call("nk_ep_destroy", self.ctx)
+        self.ctx = None
+
+
+def local_layer(full: nk.MoeWeights, rank: int, world: int) -> nk.MoeWeights:
+    """This rank's experts of `full` (weights, per-expert scales and zero
+    points sliced to experts [rank*E/G, (rank+1)*E/G)); no shared expert."""
+    E = full.experts
+    el = E // world
+
+    def sl(t, per_expert_rows=None):
+        if t is None:
+            return None
+        if per_expert_rows:  # int8 row scales [E * rows]
+            return t.reshape(E, per_expert_rows)[rank * el:(rank + 1) * el].reshape(-1)
+        return t[rank * el:(rank + 1) * el]
+
+    int8 = full.weight_kind == nk.W_INT8_ROW
+    return nk.MoeWeights(
+        hidden=full.hidden, experts=el, top_k=1, inter=full.inter, shared_inter=0,
+        route_mode=full.route_mode, weight_kind=full.weight_kind, router_w3=full.router_w3,
+        up_w=sl(full.up_w), down_w=sl(full.down_w),
+        up_scale=sl(full.up_scale, full.inter if int8 else None),
+        down_scale=sl(full.down_scale, full.hidden if int8 else None),
+        up_b=sl(full.up_b), down_b=sl(full.down_b),
+        up_zero_point=sl(full.up_zero_point), down_zero_point=sl(full.down_zero_point))
+
+
 def _tensor_at(ptr, shape, device):
     """A bf16 tensor view of device memory libnk allocated (no ownership)."""
     n = 1

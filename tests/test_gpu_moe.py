@@ -30,7 +30,8 @@ def make_layer(seed, H, E, K, I, Is, mode, kind, bias=False):
     sdown = bf16_round(r.standard_normal((H, Is)) * 0.02) if Is else None
     up_b = (r.standard_normal((E, I)) * 0.01).astype(np.float32) if bias else None
     w = nk.MoeWeights(hidden=H, experts=E, top_k=K, inter=I, shared_inter=Is, route_mode=mode,
-                      weight_kind=nk.W_BF16 if kind == "bf16" else nk.W_INT8_ROW,
+                      weight_kind={"bf16": nk.W_BF16, "int8": nk.W_INT8_ROW,
+                                   "int4": nk.W_INT4_AFFINE}[kind],
                       router_w3=nk.router_split(dev(router_w)),
                       router_b=dev(router_b) if bias else None,
                       up_b=dev(up_b) if bias else None)
@@ -41,6 +42,23 @@ def make_layer(seed, H, E, K, I, Is, mode, kind, bias=False):
         if Is:
             w.shared_up_w, w.shared_down_w = dev(sup, torch.bfloat16), dev(sdown, torch.bfloat16)
             ref.update(sup=sup, sdown=sdown)
+    elif kind == "int4":
+        # the reference's INT4-affine format per expert (scale = max|W|/7,
+        # zero point 8); the oracle runs on the dequantized weights
+        def q4(a):
+            codes, sc, zp, packed = nk.quantize_int4_experts(dev(a.reshape(-1, *a.shape[-2:])))
+            e, n, k = codes.shape[0], a.shape[-2], a.shape[-1]
+            deq = np.stack([orc.dequantize_int4(host(packed[i]), k * n, float(host(sc)[i]), 8)
+                            .reshape(k, n).T for i in range(e)])
+            return codes, sc, zp, deq.reshape(a.shape)
+        w.up_w, w.up_scale, w.up_zero_point, upd = q4(up)
+        w.down_w, w.down_scale, w.down_zero_point, downd = q4(down)
+        ref.update(up=upd, down=downd)
+        if Is:
+            c, sc, zp, ref["sup"] = q4(sup)
+            w.shared_up_w, w.shared_up_scale, w.shared_up_zero_point = c[0], sc, zp
+            c, sc, zp, ref["sdown"] = q4(sdown)
+            w.shared_down_w, w.shared_down_scale, w.shared_down_zero_point = c[0], sc, zp
     else:
         def q(a):
             rows = a.reshape(-1, a.shape[-1])
@@ -65,7 +83,7 @@ def oracle_moe(ref, x, H, E, K, I, Is, mode):
                    ref["sdown"].T.copy() if Is else None, None, x, T, mode)
 
 
-@pytest.mark.parametrize("kind", ["bf16", "int8"])
+@pytest.mark.parametrize("kind", ["bf16", "int8", "int4"])
 @pytest.mark.parametrize("T,H,E,K,I,Is,mode,bias", [
     (300, 256, 16, 4, 128, 256, nk.ROUTE_SIGMOID, False),
     (64, 512, 32, 6, 192, 0, nk.ROUTE_SIGMOID_RENORM, True),
@@ -73,6 +91,8 @@ def oracle_moe(ref, x, H, E, K, I, Is, mode):
     (700, 384, 128, 6, 144, 256, nk.ROUTE_SIGMOID_RENORM, False),
 ])
 def test_moe_matches_oracle(cuda, kind, T, H, E, K, I, Is, mode, bias):
+    if kind == "int4" and (I % 32 or H % 32 or Is % 32):
+        pytest.skip("INT4 expert rows are K/2 bytes loaded in 16-byte steps: dims % 32 == 0")
     w, ref = make_layer(T + H + E, H, E, K, I, Is, mode, kind, bias)
     x = bf16_round(rng(T).standard_normal((T, H)))
     layer = nk.MoeLayer(w)
