@@ -690,8 +690,10 @@ def config_dict(args, impl):
             "routing": "sigmoid top-6 renormalised", "weights": args.weights,
             "parallelism": (f"expert-parallel x{args.gpus}: {E // max(args.gpus, 1)} experts per "
                             "rank, routed rows exchanged by "
-                            + ("NVLink peer stores (libnk kernels)" if args.exchange == "peer"
-                               else "NCCL all-to-all-v")
+                            + {"native": "nk_moe_forward_ep (libnk: NVLink peer stores, device "
+                                         "barriers, no host sync)",
+                               "peer": "NVLink peer stores (libnk kernels, Python-ordered)",
+                               "nccl": "NCCL all-to-all-v"}[args.exchange]
                             if args.gpus > 1 else "single GPU, all experts"),
             "l2": "flushed between timed steps: 256 MiB written, then 256 MiB read (clean lines)",
             "launch": "CUDA graph of the nk_moe_forward call" if args.graph
@@ -744,22 +746,31 @@ def nk_arm(args):
                            w.up_scale.reshape(E, I)[rank * el:(rank + 1) * el].reshape(-1),
                            down_scale=None if w.down_scale is None else
                            w.down_scale.reshape(E, H)[rank * el:(rank + 1) * el].reshape(-1))
-        ep_timer = EpTimer(NkBackend(w, lw), torch)
-        if args.exchange == "nccl":
-            ep = ExpertParallelMoe(ep_timer, E, H, K)
+        if args.exchange == "native":
+            from nk_ep import NativeExpertParallelMoe, local_layer
+
+            ep = NativeExpertParallelMoe(w, local_layer(w, rank, world), max_tokens=T)
         else:
-            ep = PeerExpertParallelMoe(ep_timer, E, H, K, max_tokens=T,
-                                       phases=int(os.environ.get("NK_EP_PHASES", "1")))
+            ep_timer = EpTimer(NkBackend(w, lw), torch)
+            if args.exchange == "nccl":
+                ep = ExpertParallelMoe(ep_timer, E, H, K)
+            else:
+                ep = PeerExpertParallelMoe(ep_timer, E, H, K, max_tokens=T,
+                                           phases=int(os.environ.get("NK_EP_PHASES", "1")))
 
         def fwd():
-            out.copy_(ep.forward(x)[0])
+            if args.exchange == "native":
+                ep.forward(x, out=out, indices=idx)
+            else:
+                out.copy_(ep.forward(x)[0])
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    nk.set_stage_timing(world == 1)  # events are created during warm-up, before any capture
+    native = world > 1 and args.exchange == "native"
+    nk.set_stage_timing(world == 1 or native)  # events created during warm-up, before capture
     for _ in range(args.warmup):
         fwd()
     nk.device_status()
@@ -783,7 +794,15 @@ def nk_arm(args):
         starts[i].record(stream)
         fwd()
         ends[i].record(stream)
-        times = nk.moe_stage_times() if world == 1 else ep_timer.step_times()
+        if world == 1:
+            times = nk.moe_stage_times()
+        elif native:  # the same marks; between them the exchange phases
+            names = {"router": "router", "route_plan": "route_plan", "gather": "exchange_in",
+                     "up_proj": "up_proj", "down_proj": "down_proj_and_return",
+                     "shared_expert": "shared_wait", "combine": "combine"}
+            times = {names[k2]: v for k2, v in nk.moe_stage_times().items()}
+        else:
+            times = ep_timer.step_times()
         for kname, v in times.items():
             stage_sum[kname] = stage_sum.get(kname, 0.0) + v
     barrier()
@@ -840,6 +859,9 @@ def nk_arm(args):
     if world == 1:  # up/down stages; the shared expert runs beside them when overlapped
         grouped_ms = (stage_sum.get("up_proj", 0.0) + stage_sum.get("down_proj", 0.0) +
                       stage_sum.get("shared_expert", 0.0)) / args.steps
+    elif native:  # the down stage includes the return exchange and its barrier
+        grouped_ms = (stage_sum.get("up_proj", 0.0) +
+                      stage_sum.get("down_proj_and_return", 0.0)) / args.steps
     else:
         grouped_ms = stage_sum.get("experts", 0.0) / args.steps
     if world > 1:
@@ -858,7 +880,7 @@ def nk_arm(args):
         else:  # this rank's experts and the rows it received in the last step
             active = E // world
             rows = (int(sum(ep.last_exchange["received_rows"])) if args.exchange == "nccl"
-                    else int(ep.total.item()))
+                    else ep.received_rows() if native else int(ep.total.item()))
         expert_w_bytes = active * 2 * I * H * wbytes_per
         act_bytes = rows * H * 2 + 2 * rows * I * 2 + rows * H * 2
         grouped_bytes = expert_w_bytes + act_bytes
@@ -901,11 +923,13 @@ def nk_arm(args):
             "e2e": {"value": tokens_total / (total_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
             "clocks": clocks,
-            # libnk launches per forward: one GPU 13 (router GEMM + reduce, route,
-            # plan count / scan / place, gather, tile lists, up, down, shared up /
-            # down, combine); expert-parallel 15 (no gather; exchange plan,
-            # dispatch and return instead)
-            "gpu_launches": (13 if world == 1 else 15) * args.steps * 2,
+            # libnk kernels per forward: one GPU 16 (router GEMM, router norms,
+            # candidates, rescore, selection, plan count / scan / place, gather,
+            # tile lists, up, down, shared up / down, combine); native expert
+            # parallel 21 (no gather; counts exchange, exchange plan, capacity
+            # check, dispatch, 2 barriers and return instead); the Python-ordered
+            # exchanges 17.  Timed region: K steps, then K e2e steps.
+            "gpu_launches": ({1: 16}.get(world, 21 if native else 17)) * args.steps * 2,
         }
         line["e2e"]["how"] = (
             "nk_moe_pipeline_submit per step (host-buffer executor: pinned x in, f32 out back; "
@@ -951,6 +975,8 @@ def nk_arm(args):
                                          "4096-token batch)"}}
         print_json(line)
     if world > 1:
+        if native:
+            ep.close()
         torch.distributed.destroy_process_group()
     return 0
 
@@ -979,9 +1005,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=T,
                     help="tokens per GPU (profiling captures use a smaller case)")
     ap.add_argument("--experts", type=int, default=E)
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
-                    help="expert-parallel row exchange: NVLink peer stores (libnk kernels) "
-                         "or NCCL all-to-all-v")
+    ap.add_argument("--exchange", choices=["native", "peer", "nccl"], default="native",
+                    help="expert-parallel exchange: the native C-ABI executor (default), the "
+                         "Python-ordered peer-store exchange, or NCCL all-to-all-v")
     ap.add_argument("--tp", action="store_true",
                     help="also time config 4's tensor-parallel projections")
     ap.add_argument("--sweep", action="store_true",

@@ -296,7 +296,15 @@ typedef struct nk_moe_layer {
   const uint8_t *down_zero_point;        /* [E] */
   const uint8_t *shared_up_zero_point;   /* [1] */
   const uint8_t *shared_down_zero_point; /* [1] */
+  /* [2E]: |W_e|_2 and |lo_e|_2 of the router weight (nk_router_norms), which
+   * bound the tensor-core router's error; NULL: computed on every call. */
+  const float *router_norms;
 } nk_moe_layer;
+
+/* The router weight's per-expert norms for nk_moe_layer.router_norms: once
+ * per layer, after nk_router_split (norms: [2E] f32). */
+nk_status nk_router_norms(const uint16_t *router_w3, int64_t experts, int64_t hidden,
+                          float *norms, void *stream);
 
 /* Splits a router weight f32 [E,H] into the [E, 3*Hp] bf16 triple used by
  * nk_moe_forward (hi | mid | lo, each zero padded to Hp = ceil(H/64)*64;

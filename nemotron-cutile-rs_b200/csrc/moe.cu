@@ -76,18 +76,6 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
   }
 }
 
-// Xp[pos, :] = x[perm[pos] / top_k, :]  (16-byte vectors; H % 8 == 0).
-__global__ void gather_rows_kernel(const uint4 *__restrict__ x, const int32_t *__restrict__ perm,
-                                   int64_t slots, int top_k, int64_t row_vecs,
-                                   uint4 *__restrict__ xp) {
-  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (pos >= slots) return;
-  const int64_t t = perm[pos] / top_k;
-  const uint4 *src = x + t * row_vecs;
-  uint4 *dst = xp + pos * row_vecs;
-  for (int64_t v = threadIdx.x & 31; v < row_vecs; v += 32) dst[v] = src[v];
-}
-
 // out[t, c] = 0 (+ shared[t, c]) + Σ_r w[t, r] * y[slot_pos[t*k + r], c], each
 // product and sum rounded in f32 in rank order (moe.rs:195-246).  One block per
 // token; each thread owns 8 consecutive columns (16-byte loads; H % 8 == 0).
@@ -204,15 +192,12 @@ struct Carver {
 struct DispatchWs {
   float *router_partial;
   void *route_scratch;
-  int32_t *perm, *plan_scratch;
 };
 DispatchWs carve_dispatch(const nk_moe_layer &L, int64_t T, Carver &c) {
-  const int64_t E = L.experts, S = T * L.top_k;
+  const int64_t E = L.experts;
   DispatchWs w;
   w.router_partial = (float *)c.take(sizeof(float) * T * E * kRouterMaxSplits);
-  w.route_scratch = c.take(route_exact_scratch_bytes(T, E));
-  w.perm = (int32_t *)c.take(sizeof(int32_t) * S);
-  w.plan_scratch = (int32_t *)c.take(plan_scratch_bytes(S, E));
+  w.route_scratch = c.take(route_exact_scratch_bytes(T, E, (int)L.top_k));
   return w;
 }
 
@@ -404,7 +389,7 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
                          float *rw, int32_t *counts, int32_t *offsets, int32_t *slot_pos,
                          uint16_t *xp, const DispatchWs &ws, StageTimer &tm, cudaStream_t s) {
   int *err = device_error_ptr();
-  const int64_t E = L.experts, K = L.top_k, H = L.hidden, S = T * K;
+  const int64_t E = L.experts, K = L.top_k, H = L.hidden;
   nk_status st;
   tm.mark(0, s);
   // router scores [T, E] f32: x · (hi + mid)ᵀ.  K is split over CTAs into f32
@@ -445,19 +430,13 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
     router_splits = splits;
   }
   tm.mark(1, s);
+  // routes, the expert plan and (xp) the routed rows copied into expert order;
+  // without xp the rows are moved elsewhere (expert-parallel dispatch)
   st = launch_route_exact(ws.router_partial, router_splits, x, T, (int)H, L.router_w3,
-                          L.router_b, c_bound, (int)E, (int)K, L.route_mode, ws.route_scratch,
-                          idx, rw, s);
-  if (st != NK_OK) return st;
-  st = launch_plan(idx, S, (int)E, counts, offsets, ws.perm, slot_pos, ws.plan_scratch, s);
-  if (st != NK_OK) return st;
+                          L.router_b, L.router_norms, c_bound, (int)E, (int)K, L.route_mode,
+                          ws.route_scratch, idx, rw, counts, offsets, slot_pos, xp, s);
   tm.mark(2, s);
-  if (!xp) return NK_OK;  // rows are gathered elsewhere (expert-parallel dispatch)
-  const int warps = 8;
-  gather_rows_kernel<<<(unsigned)ceil_div(S, warps), warps * 32, 0, s>>>(
-      reinterpret_cast<const uint4 *>(x), ws.perm, S, (int)K, H / 8,
-      reinterpret_cast<uint4 *>(xp));
-  return check_launch("gather_rows_kernel");
+  return st;
 }
 
 // Grouped expert MLP over R rows laid out as n_seg back-to-back segments:
@@ -899,6 +878,15 @@ nk_status nk_moe_forward_ep(nk_ep_ctx *ctx, const nk_moe_layer *layer, const nk_
   if (out_dtype != NK_F32 && out_dtype != NK_BF16) return fail(NK_UNSUPPORTED, "out_dtype");
   st = moe_forward_ep(ctx, *layer, *local, x, tokens, out, out_dtype, indices, weights,
                       workspace, workspace_bytes, as_stream(stream));
+  return st == NK_OK ? ok() : st;
+}
+
+
+nk_status nk_router_norms(const uint16_t *router_w3, int64_t experts, int64_t hidden,
+                          float *norms, void *stream) {
+  if (experts <= 0 || hidden <= 0) return fail(NK_INVALID_SHAPE, "experts and hidden > 0");
+  if (!router_w3 || !norms) return fail(NK_INVALID_PARAMS, "router_w3 and norms");
+  nk_status st = launch_router_norms(router_w3, experts, hidden, norms, as_stream(stream));
   return st == NK_OK ? ok() : st;
 }
 

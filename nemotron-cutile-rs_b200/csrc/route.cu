@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32)
 constexpr int kCandCap = 16;
 constexpr int kRouterMaxSplits = 16;  // the router GEMM's split-K limit
 constexpr int kCandWarps = 4;
+constexpr int kSelWarps = 8;  // tokens per block of kernel C = tokens per plan chunk
 constexpr int kRescoreWarps = 8;
 constexpr int kRescoreBatch = 4;  // tokens per warp pass in kernel B
 
@@ -609,18 +610,16 @@ __global__ void __launch_bounds__(kRescoreWarps * 32)
   }
 }
 
-// Kernel C.  Shared memory per warp: keys, values, candidates [Ep], taken [Ep/32].
-__global__ void __launch_bounds__(kCandWarps * 32)
-    route_select_kernel(const __nv_bfloat16 *__restrict__ x, int64_t tokens, int H,
-                        const __nv_bfloat16 *__restrict__ w3, int64_t hp,
-                        const float *__restrict__ bias, int E, int K, int mode, ExactRouteWs ws,
-                        int32_t *__restrict__ indices, float *__restrict__ weights) {
-  extern __shared__ int32_t sel_sm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * kCandWarps + warp;
-  if (t >= tokens) return;
+// One token of kernel C: top-k over its candidates' exact scores.  sel
+// (shared memory, 32 ints) receives the k selected experts in rank order.
+__device__ void route_select_token(const __nv_bfloat16 *__restrict__ x, int64_t t, int H,
+                                   const __nv_bfloat16 *__restrict__ w3, int64_t hp,
+                                   const float *__restrict__ bias, int E, int K, int mode,
+                                   const ExactRouteWs &ws, int32_t *__restrict__ indices,
+                                   float *__restrict__ weights, int32_t *smem, int32_t *sel,
+                                   int lane) {
   const int Ep = (E + 31) & ~31, words = Ep / 32;
-  int32_t *key = sel_sm + (int64_t)warp * (3 * Ep + words);
+  int32_t *key = smem;
   float *val = reinterpret_cast<float *>(key + Ep);
   int32_t *cand = key + 2 * Ep;
   uint32_t *tk = reinterpret_cast<uint32_t *>(key + 3 * Ep);
@@ -677,28 +676,99 @@ __global__ void __launch_bounds__(kCandWarps * 32)
   }
   if (lane == 0) {
     if (mode == NK_ROUTE_SOFTMAX || mode == NK_ROUTE_SIGMOID_RENORM) {
-      float sel = -0.0f;
-      for (int r = 0; r < K; ++r) sel = __fadd_rn(sel, sel_w[r]);
-      for (int r = 0; r < K; ++r) sel_w[r] = __fdiv_rn(sel_w[r], sel);
+      float total = -0.0f;
+      for (int r = 0; r < K; ++r) total = __fadd_rn(total, sel_w[r]);
+      for (int r = 0; r < K; ++r) sel_w[r] = __fdiv_rn(sel_w[r], total);
     }
     for (int r = 0; r < K; ++r) {
       indices[t * K + r] = sel_i[r];
       weights[t * K + r] = sel_w[r];
+      sel[r] = sel_i[r];
     }
   }
 }
 
-size_t route_exact_scratch_bytes(int64_t tokens, int64_t E) {
+// Kernel C.  A block of kSelWarps tokens is one chunk of the expert plan:
+// besides the routes it writes the chunk's per-expert histogram
+// (chunk_counts[block][e]) and each slot's rank among the chunk's slots of
+// the same expert in slot order (slot_rank), so the expert-ordered position
+// of a slot is offsets[e] + (slots of expert e in earlier chunks) + rank: the
+// stable (token, rank) order of the reference's per-expert loops.
+// Shared memory: per warp keys, values, candidates [Ep], taken [Ep/32]; then
+// the block's histogram [E] and its selections [kSelWarps][K].
+__global__ void __launch_bounds__(kSelWarps * 32)
+    route_select_kernel(const __nv_bfloat16 *__restrict__ x, int64_t tokens, int H,
+                        const __nv_bfloat16 *__restrict__ w3, int64_t hp,
+                        const float *__restrict__ bias, int E, int K, int mode, ExactRouteWs ws,
+                        int32_t *__restrict__ indices, float *__restrict__ weights,
+                        int32_t *__restrict__ chunk_counts, int32_t *__restrict__ slot_rank) {
+  extern __shared__ int32_t sel_sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kSelWarps + warp;
+  const int Ep = (E + 31) & ~31, words = Ep / 32;
+  int32_t *hist = sel_sm + kSelWarps * (3 * Ep + words);
+  int32_t *bsel = hist + Ep;  // [kSelWarps][32]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  for (int i = threadIdx.x; i < kSelWarps * 32; i += blockDim.x) bsel[i] = -1;
+  __syncthreads();
+  if (t < tokens) route_select_token(x, t, H, w3, hp, bias, E, K, mode, ws, indices, weights,
+                                     sel_sm + (int64_t)warp * (3 * Ep + words), bsel + warp * 32,
+                                     lane);
+  __syncthreads();
+  // histogram and ranks of the block's slots
+  if (t < tokens && lane < K) {
+    const int e = bsel[warp * 32 + lane];
+    atomicAdd(&hist[e], 1);
+    int rank = 0;
+    for (int w2 = 0; w2 < warp; ++w2)
+      for (int r = 0; r < K; ++r) rank += bsel[w2 * 32 + r] == e;
+    slot_rank[t * K + lane] = rank;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    chunk_counts[(int64_t)blockIdx.x * E + e] = hist[e];
+}
+
+__global__ void plan_scan_kernel(int32_t *__restrict__ chunk_counts, int nchunks, int E,
+                                 int32_t *__restrict__ counts, int32_t *__restrict__ offsets);
+
+// Expert-ordered position of every route slot (offsets[e] + the chunk's base
+// for e + the slot's rank in its chunk); optionally the token row copied there.
+__global__ void scatter_rows_kernel(const uint4 *__restrict__ x, const int32_t *__restrict__ idx,
+                                    const int32_t *__restrict__ slot_rank,
+                                    const int32_t *__restrict__ chunk_base,
+                                    const int32_t *__restrict__ offsets, int64_t slots, int K,
+                                    int E, int64_t row_vecs, int32_t *__restrict__ slot_pos,
+                                    uint4 *__restrict__ xp) {
+  const int64_t s = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (s >= slots) return;
+  const int64_t t = s / K, c = t / kSelWarps;
+  const int e = idx[s];
+  const int64_t pos = offsets[e] + chunk_base[c * E + e] + slot_rank[s];
+  if ((threadIdx.x & 31) == 0) slot_pos[s] = (int32_t)pos;
+  if (!xp) return;
+  const uint4 *src = x + t * row_vecs;
+  uint4 *dst = xp + pos * row_vecs;
+  for (int64_t v = threadIdx.x & 31; v < row_vecs; v += 32) dst[v] = src[v];
+}
+
+size_t route_exact_scratch_bytes(int64_t tokens, int64_t E, int K) {
   auto a = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const int64_t chunks = ceil_div(tokens, kSelWarps);
   return 2 * a(4 * E) + a(4 * tokens) + a(4 * tokens) + 2 * a(4 * tokens * kCandCap) + a(4 * E) +
-         a(4 * E * tokens);
+         a(4 * E * tokens) + a(4 * tokens * K) + a(4 * chunks * E);
 }
 
 nk_status launch_route_exact(const float *partial, int splits, const uint16_t *x,
                              int64_t tokens, int H, const uint16_t *w3, const float *bias,
-                             float c, int E, int K, int mode, void *scratch, int32_t *indices,
-                             float *weights, cudaStream_t stream) {
-  if (tokens == 0) return ok();
+                             const float *norms, float c, int E, int K, int mode, void *scratch,
+                             int32_t *indices, float *weights, int32_t *counts, int32_t *offsets,
+                             int32_t *slot_pos, uint16_t *xp, cudaStream_t stream) {
+  if (tokens == 0) {
+    NK_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream));
+    NK_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), stream));
+    return ok();
+  }
   auto a = [](size_t v) { return (v + 255) & ~size_t(255); };
   uint8_t *p = reinterpret_cast<uint8_t *>(scratch);
   ExactRouteWs ws;
@@ -709,19 +779,27 @@ nk_status launch_route_exact(const float *partial, int splits, const uint16_t *x
   ws.cand = (int32_t *)p; p += a(4 * tokens * kCandCap);
   ws.exact = (float *)p; p += a(4 * tokens * kCandCap);
   ws.e_count = (int32_t *)p; p += a(4 * E);
-  ws.pairs = (int32_t *)p;
+  ws.pairs = (int32_t *)p; p += a(4 * E * tokens);
+  int32_t *slot_rank = (int32_t *)p; p += a(4 * tokens * K);
+  int32_t *chunk_counts = (int32_t *)p;
   const int64_t hp = ceil_div(H, 64) * 64;
   const __nv_bfloat16 *w = reinterpret_cast<const __nv_bfloat16 *>(w3);
   const __nv_bfloat16 *xb = reinterpret_cast<const __nv_bfloat16 *>(x);
   NK_CUDA_TRY(cudaMemsetAsync(ws.e_count, 0, sizeof(int32_t) * E, stream));
-  router_wnorm_kernel<<<(unsigned)E, 256, 0, stream>>>(w, hp, H, ws.wnorm, ws.lonorm);
-  nk_status st = check_launch("router_wnorm_kernel");
-  if (st != NK_OK) return st;
+  nk_status st;
+  if (norms) {  // precomputed by nk_router_norms: |W_e|_2 then |lo_e|_2
+    ws.wnorm = const_cast<float *>(norms);
+    ws.lonorm = const_cast<float *>(norms) + E;
+  } else {
+    router_wnorm_kernel<<<(unsigned)E, 256, 0, stream>>>(w, hp, H, ws.wnorm, ws.lonorm);
+    st = check_launch("router_wnorm_kernel");
+    if (st != NK_OK) return st;
+  }
   const int ep = (E + 31) & ~31;
-  const unsigned tok_blocks = (unsigned)ceil_div(tokens, kCandWarps);
-  const size_t smem_c = sizeof(int32_t) * kCandWarps * (3 * ep + ep / 32);
-  const size_t smem_b =
-      sizeof(double) * ((size_t)(((H >> 3) + 31) >> 5) * 256 + 8);
+  const unsigned cand_blocks = (unsigned)ceil_div(tokens, kCandWarps);
+  const unsigned sel_blocks = (unsigned)ceil_div(tokens, kSelWarps);
+  const size_t smem_c = sizeof(int32_t) * (kSelWarps * (3 * ep + ep / 32) + ep + kSelWarps * 32);
+  const size_t smem_b = sizeof(double) * ((size_t)(((H >> 3) + 31) >> 5) * 256 + 8);
   if (smem_b > 200 * 1024) return fail(NK_UNSUPPORTED, "exact routing needs hidden <= 25000");
   if (smem_b > 48 * 1024)
     NK_CUDA_TRY(cudaFuncSetAttribute(route_rescore_kernel,
@@ -732,8 +810,8 @@ nk_status launch_route_exact(const float *partial, int splits, const uint16_t *x
   {
     const int epl = (E + 31) / 32;
     auto launch = [&](auto kern) {
-      kern<<<tok_blocks, kCandWarps * 32, 0, stream>>>(partial, splits, tokens * E, xb, tokens, H,
-                                                      bias, c, E, K, mode, ws);
+      kern<<<cand_blocks, kCandWarps * 32, 0, stream>>>(partial, splits, tokens * E, xb, tokens,
+                                                        H, bias, c, E, K, mode, ws);
     };
     if (epl <= 1) launch(route_cand_kernel<1>);
     else if (epl <= 2) launch(route_cand_kernel<2>);
@@ -755,9 +833,30 @@ nk_status launch_route_exact(const float *partial, int splits, const uint16_t *x
     st = check_launch("route_rescore_kernel");
     if (st != NK_OK) return st;
   }
-  route_select_kernel<<<tok_blocks, kCandWarps * 32, smem_c, stream>>>(
-      xb, tokens, H, w, hp, bias, E, K, mode, ws, indices, weights);
-  return check_launch("route_select_kernel");
+  route_select_kernel<<<sel_blocks, kSelWarps * 32, smem_c, stream>>>(
+      xb, tokens, H, w, hp, bias, E, K, mode, ws, indices, weights, chunk_counts, slot_rank);
+  st = check_launch("route_select_kernel");
+  if (st != NK_OK) return st;
+  // chunk histograms -> per-chunk bases (in place), counts, offsets
+  int threads = 32;
+  while (threads < E) threads <<= 1;
+  plan_scan_kernel<<<1, threads, 0, stream>>>(chunk_counts, (int)sel_blocks, E, counts, offsets);
+  st = check_launch("plan_scan_kernel");
+  if (st != NK_OK) return st;
+  const int64_t slots = tokens * K;
+  const int warps = 8;
+  scatter_rows_kernel<<<(unsigned)ceil_div(slots, warps), warps * 32, 0, stream>>>(
+      reinterpret_cast<const uint4 *>(x), indices, slot_rank, chunk_counts, offsets, slots, K, E,
+      H / 8, slot_pos, reinterpret_cast<uint4 *>(xp));
+  return check_launch("scatter_rows_kernel");
+}
+
+nk_status launch_router_norms(const uint16_t *w3, int64_t E, int64_t H, float *norms,
+                              cudaStream_t stream) {
+  const int64_t hp = ceil_div(H, 64) * 64;
+  router_wnorm_kernel<<<(unsigned)E, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(w3), hp, (int)H, norms, norms + E);
+  return check_launch("router_wnorm_kernel");
 }
 
 // ------------------------------------------------------------------- plan

@@ -68,6 +68,7 @@ class NkMoeLayer(_c.Structure):
         ("shared_down_w", _p), ("shared_down_scale", _p), ("shared_down_b", _p),
         ("up_zero_point", _p), ("down_zero_point", _p),
         ("shared_up_zero_point", _p), ("shared_down_zero_point", _p),
+        ("router_norms", _p),
     ]
 
 
@@ -140,6 +141,7 @@ _SIGS = {
     "nk_unpack_int4": (_i32, [_p, _sz, _sz, _p, _sz, _p]),
     "nk_quantize_int4": (_i32, [_p, _sz, _f, _u32, _p, _sz, _p]),
     "nk_int4_kn_to_nk": (_i32, [_p, _i64, _i64, _i64, _p, _p]),
+    "nk_router_norms": (_i32, [_p, _i64, _i64, _p, _p]),
     "nk_dequantize_int4": (_i32, [_p, _sz, _sz, _f, _u32, _p, _sz, _p]),
     "nk_validate_int4_params": (_i32, [_f, _u32]),
     "nk_quantize_int8_row": (_i32, [_p, _i64, _i64, _p, _p, _p]),
@@ -444,6 +446,7 @@ class MoeWeights:
     down_zero_point: object = None
     shared_up_zero_point: object = None   # uint8 [1]
     shared_down_zero_point: object = None
+    router_norms: object = None           # f32 [2E] (nk_router_norms), or computed per call
 
     def struct(self) -> NkMoeLayer:
         s = NkMoeLayer()
@@ -453,15 +456,27 @@ class MoeWeights:
         for f in ("router_w3", "router_b", "up_w", "up_scale", "up_b", "down_w", "down_scale",
                   "down_b", "shared_up_w", "shared_up_scale", "shared_up_b", "shared_down_w",
                   "shared_down_scale", "shared_down_b", "up_zero_point", "down_zero_point",
-                  "shared_up_zero_point", "shared_down_zero_point"):
+                  "shared_up_zero_point", "shared_down_zero_point", "router_norms"):
             setattr(s, f, ptr(getattr(self, f)))
         return s
+
+
+def ensure_router_norms(weights: MoeWeights) -> None:
+    """Fills weights.router_norms once (nk_router_norms) so that forwards skip it."""
+    import torch
+
+    if weights.router_norms is None and weights.router_w3 is not None:
+        weights.router_norms = torch.empty(2 * weights.experts, dtype=torch.float32,
+                                           device=weights.router_w3.device)
+        call("nk_router_norms", ptr(weights.router_w3), weights.experts, weights.hidden,
+             ptr(weights.router_norms), stream_ptr())
 
 
 class MoeLayer:
     """Device MoE layer: MoeLayer::forward_into (nemotron-nn/src/moe.rs:154-249)."""
 
     def __init__(self, weights: MoeWeights):
+        ensure_router_norms(weights)
         self.weights = weights
         self._struct = weights.struct()
         self._ws = None

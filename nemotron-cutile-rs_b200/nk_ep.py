@@ -45,6 +45,7 @@ class NkBackend:
     stacked in local order).  Both are nk.MoeWeights."""
 
     def __init__(self, dispatch_layer: nk.MoeWeights, local_layer: nk.MoeWeights):
+        nk.ensure_router_norms(dispatch_layer)
         self.d = dispatch_layer
         self.l = local_layer
         self._ds = dispatch_layer.struct()
@@ -346,6 +347,7 @@ class NativeExpertParallelMoe:
         self.G = dist.get_world_size(group)
         self.me = dist.get_rank(group)
         self.T_max = max_tokens
+        nk.ensure_router_norms(full)
         self._fs, self._ls = full.struct(), local.struct()
         nbytes = nk.lib().nk_ep_handle_bytes()
         blob = (C.c_uint8 * nbytes)()
