@@ -163,6 +163,7 @@ __global__ void ep_capacity_kernel(int32_t *total, int64_t cap, int *err) {
 }
 
 static uint64_t *table(const nk_ep_ctx *c, int which) { return c->tables + which * c->ranks; }
+const uint64_t *ep_out_table(const nk_ep_ctx *c) { return table(c, 1); }
 
 uint16_t *ep_recv(const nk_ep_ctx *c) { return reinterpret_cast<uint16_t *>(c->block); }
 uint16_t *ep_out(const nk_ep_ctx *c) {

@@ -33,4 +33,6 @@ nk_status ep_plan(nk_ep_ctx *c, cudaStream_t s);
 nk_status ep_dispatch(nk_ep_ctx *c, const uint16_t *x, int64_t tokens, const int32_t *idx,
                       const int32_t *slot_pos, const int32_t *offsets, cudaStream_t s);
 nk_status ep_return(nk_ep_ctx *c, cudaStream_t s);
+// Device table of the ranks' result buffers (uint64 addresses, rank order).
+const uint64_t *ep_out_table(const nk_ep_ctx *c);
 }  // namespace nk

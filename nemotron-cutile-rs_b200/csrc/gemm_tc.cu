@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
   constexpr int kEpiWarps = Cfg::kEpiThreads / 32;
   constexpr int S = Cfg::kStages;
   constexpr int FH = Cfg::kFeatRows;
+  constexpr int KB = Cfg::kKB;
   constexpr bool kQuant = WK != WK_BF16;
   constexpr int R = Cfg::kRawSlots > 0 ? Cfg::kRawSlots : 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         while ((uint32_t)token_box_rows(x_map) < n_mma / PAIR) ++x_map;
         const uint32_t x_box = token_box_rows(x_map);
         int r_start = 0;  // first K block of the current raw group
-        for (int kk = 0; kk < k_count; ++kk) {
+        for (int kk = 0; kk < k_count; kk += KB) {
           if (*abort_v || !mbar_wait(&empty[stage], phase ^ 1, err)) {
             ok = false;
             break;
@@ -214,11 +215,23 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
           const int kb = k_begin + kk;
           const int wkb = args.w_k_period > 0 ? kb % args.w_k_period : kb;
           const int xkb = args.x_k_period > 0 ? kb % args.x_k_period : kb;
+          const int nb = k_count - kk < KB ? k_count - kk : KB;  // K blocks in this stage
           // Token tile (and bf16 weight tile) complete on the leader's `full`.
           if (leader)
             mbar_arrive_expect_tx(&full[stage],
-                                  PAIR * ((kQuant ? 0 : Cfg::kATileBytes * n_a) + x_box * 128));
-          if (PAIR == 2) {
+                                  PAIR * nb * ((kQuant ? 0 : Cfg::kATileBytes * n_a) + x_box * 128));
+          if (KB > 1) {  // single CTAs, one accumulator
+            for (int b = 0; b < nb; ++b) {
+              const int kb2 = kb + b;
+              const int wk2 = args.w_k_period > 0 ? kb2 % args.w_k_period : kb2;
+              const int xk2 = args.x_k_period > 0 ? kb2 % args.x_k_period : kb2;
+              if (!kQuant)
+                tma_load_2d(a_tiles + stage * Cfg::kABytes + b * Cfg::kATileBytes, &wmap,
+                            &full[stage], wk2 * 64, a_row);
+              tma_load_2d(b_tiles + stage * Cfg::kBBytes + b * Cfg::kBTileBytes,
+                          &xmaps.m[x_map], &full[stage], xk2 * 64, b_row);
+            }
+          } else if (PAIR == 2) {
             const uint32_t fb = leader_bar(&full[stage]);
             if (!kQuant)
               tma_load_2d_pair(a_tiles + stage * Cfg::kABytes, &wmap, fb, wkb * 64, a_row);
@@ -237,15 +250,15 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
             stage = 0;
             phase ^= 1;
           }
-          if (kQuant) {  // the item ends a raw group: top the raw ring up by one group
-            if (kk == r_start + raw_group_len(G, r_start, k_begin, k_count, args.w_k_period) - 1) {
-              r_start = kk + 1;
-              if (!issue_raw()) {
-                ok = false;
-                break;
-              }
+          // each K block of the stage that ends a raw group tops the raw ring up by one group
+          for (int b = 0; kQuant && b < nb && ok; ++b) {
+            const int kkb = kk + b;
+            if (kkb == r_start + raw_group_len(G, r_start, k_begin, k_count, args.w_k_period) - 1) {
+              r_start = kkb + 1;
+              ok = issue_raw();
             }
           }
+          if (!ok) break;
         }
       }
       if (!ok) *abort_v = 1;
@@ -278,7 +291,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * FA * BN);
-        for (int kb = 0; kb < k_count; ++kb) {
+        for (int kb = 0; kb < k_count; kb += KB) {
           bool got = mbar_wait(&full[stage], phase, err);
           if (kQuant && got) got = mbar_wait(&conv[stage], phase, err);
           if (*abort_v || !got) {
@@ -288,7 +301,19 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
           // (the mbarrier wait orders the TMA-written operands for the MMA; no
           // tcgen05 fence is needed per stage)
           const uint64_t bd = smem_desc_sw128(b_base + stage * Cfg::kBBytes);
-          for (int ai = 0; ai < n_a; ++ai) {
+          if (KB > 1) {
+            const int nb = k_count - kb < KB ? k_count - kb : KB;
+            for (int b = 0; b < nb; ++b) {
+              const uint64_t ad2 =
+                  smem_desc_sw128(a_base + stage * Cfg::kABytes + b * Cfg::kATileBytes);
+              const uint64_t bd2 =
+                  smem_desc_sw128(b_base + stage * Cfg::kBBytes + b * Cfg::kBTileBytes);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                tc_mma_bf16(d_tmem, ad2 + 2 * j, bd2 + 2 * j, idesc, (kb | b | j) != 0);
+            }
+          }
+          for (int ai = 0; ai < (KB > 1 ? 0 : n_a); ++ai) {
             const uint64_t ad =
                 smem_desc_sw128(a_base + stage * Cfg::kABytes + ai * Cfg::kATileBytes);
 #pragma unroll
@@ -391,8 +416,11 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
         if (frow) {
-          __nv_bfloat16 *yb = reinterpret_cast<__nv_bfloat16 *>(args.y) + tile.out_col0 + fi +
-                              (long long)split * args.split_stride;
+          __nv_bfloat16 *yb = reinterpret_cast<__nv_bfloat16 *>(
+                                  tile.y_rank >= 0 ? reinterpret_cast<void *>(args.y_peers[tile.y_rank])
+                                                   : args.y) +
+                              tile.out_col0 + fi + (long long)split * args.split_stride;
+          const int row0 = tile.y_rank >= 0 ? tile.y_row : tile.x_row;
 #pragma unroll
           for (int c = 0; c < BN / 16; ++c) {
             if (c < chunks) {
@@ -402,13 +430,16 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
                 if (j < t_valid) {
                   const uint32_t w = pk[c * 8 + (jj >> 1)];
                   const unsigned short h = (jj & 1) ? (unsigned short)(w >> 16) : (unsigned short)w;
-                  reinterpret_cast<unsigned short *>(yb)[(long long)(tile.x_row + j) * args.ldy] = h;
+                  reinterpret_cast<unsigned short *>(yb)[(long long)(row0 + j) * args.ldy] = h;
                 }
               }
             }
           }
+          if (tile.y_rank >= 0) __threadfence_system();  // peer stores before the next barrier
         }
       } else {
+        void *ybase = tile.y_rank >= 0 ? reinterpret_cast<void *>(args.y_peers[tile.y_rank]) : args.y;
+        const int row0 = tile.y_rank >= 0 ? tile.y_row : tile.x_row;
         for (int c = 0; c < chunks; ++c) {
           float v[16];
           tmem_ld16(taddr + c * 16, v);
@@ -420,16 +451,17 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
                 float o = v[jj] * mul + add;
                 if (args.relu2) o = nk_relu2(o);
                 if (args.tok_scale) o *= args.tok_scale[tile.x_row + j];
-                const long long off = (long long)(tile.x_row + j) * args.ldy + tile.out_col0 +
-                                      fi + split * args.split_stride;
+                const long long off = (long long)(row0 + j) * args.ldy + tile.out_col0 + fi +
+                                      split * args.split_stride;
                 if (args.y_f32)
-                  reinterpret_cast<float *>(args.y)[off] = o;
+                  reinterpret_cast<float *>(ybase)[off] = o;
                 else
-                  reinterpret_cast<__nv_bfloat16 *>(args.y)[off] = __float2bfloat16_rn(o);
+                  reinterpret_cast<__nv_bfloat16 *>(ybase)[off] = __float2bfloat16_rn(o);
               }
             }
           }
         }
+        if (tile.y_rank >= 0) __threadfence_system();  // peer stores before the next barrier
         tc_fence_before();
         if (PAIR == 2)
           mbar_arrive_cluster(leader_bar(&tempty[acc]));
@@ -461,15 +493,21 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
       if (WK == WK_INT4NK && args.group_zp) zp = (int)args.group_zp[a_row / args.group_rows];
       const float zbias = WK == WK_INT8 ? 8388736.0f : 8388608.0f + (float)zp;  // 2^23 + bias
       int r_start = 0, r_len = raw_group_len(G, 0, k_begin, k_count, args.w_k_period);
-      for (int kb = 0; kb < k_count; ++kb) {
+      for (int ks = 0; ks < k_count && ok; ks += KB) {
+        if (*abort_v || !mbar_wait_backoff(&empty[stage], phase ^ 1, err)) {
+          ok = false;
+          break;
+        }
+        const int nb = k_count - ks < KB ? k_count - ks : KB;
+       for (int b = 0; b < nb; ++b) {
+        const int kb = ks + b;
         const int g = kb - r_start;  // K block within the raw tile
-        if (*abort_v || (g == 0 && !mbar_wait_backoff(&rawfull[rslot], rphase, err)) ||
-            !mbar_wait_backoff(&empty[stage], phase ^ 1, err)) {
+        if (*abort_v || (g == 0 && !mbar_wait_backoff(&rawfull[rslot], rphase, err))) {
           ok = false;
           break;
         }
         const uint8_t *raw = raw_tiles + rslot * Cfg::kRawTileBytes + (WK == WK_INT4KN ? g * RB : 0);
-        uint8_t *dst = a_tiles + stage * Cfg::kABytes;
+        uint8_t *dst = a_tiles + stage * Cfg::kABytes + b * Cfg::kATileBytes;
 #pragma unroll
         for (int q = 0; q < 1024 / kTT; ++q) {
           const int idx = q * kTT + tid;
@@ -527,14 +565,21 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
           *reinterpret_cast<uint4 *>(dst + row * 128 + ((c ^ (row & 7)) << 4)) =
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
-        fence_proxy_async_smem();
         const bool last = g == r_len - 1;
         if (last) {
+          fence_proxy_async_smem();  // our reads of the raw slot before its next TMA write
           mbar_arrive(&rawempty[rslot]);
           r_start = kb + 1;
           if (r_start < k_count)
             r_len = raw_group_len(G, r_start, k_begin, k_count, args.w_k_period);
+          if (++rslot == R) {
+            rslot = 0;
+            rphase ^= 1;
+          }
         }
+       }
+        if (!ok) break;
+        fence_proxy_async_smem();
         if (PAIR == 2)
           mbar_arrive_cluster(leader_bar(&conv[stage]));
         else
@@ -542,10 +587,6 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
-        }
-        if (last && ++rslot == R) {
-          rslot = 0;
-          rphase ^= 1;
         }
       }
     }

@@ -36,10 +36,12 @@ enum WeightKind { WK_BF16 = 0, WK_INT8 = 1, WK_INT4KN = 2, WK_INT4NK = 3 };
 
 
 struct TcTile {  // one output tile: 128 (256 for CTA pairs) features x up to BN tokens
-  int w_row;     // first weight row (feature) in the weight tensor map
-  int x_row;     // first activation row in the activation tensor map
-  int valid;     // (f_valid << 16) | t_valid
-  int out_col0;  // output column of feature 0 of the tile
+  int w_row;       // first weight row (feature) in the weight tensor map
+  int x_row;       // first activation row in the activation tensor map
+  int valid;       // (f_valid << 16) | t_valid
+  int out_col0;    // output column of feature 0 of the tile
+  int y_row = 0;   // y_rank >= 0: output row of token 0 in rank y_rank's buffer
+  int y_rank = -1; // -1: output row x_row + j of args.y
 };
 
 struct TcArgs {
@@ -61,6 +63,7 @@ struct TcArgs {
   const float *row_scale;   // [features] per weight row (INT8 row scale) or null
   const float *bias;        // [features] or null
   const float *tok_scale;   // [activation rows] per token (routing weight) or null
+  const uint64_t *y_peers;  // tiles with y_rank >= 0: output buffers by rank (peer memory)
   int relu2;
   int w_zero_point;         // INT4 zero point
   // per-group (expert) INT4 parameters: group g = weight row / group_rows
@@ -107,10 +110,17 @@ struct TcConfig {
   static_assert(FA == 1 || (FA == 2 && PAIR == 1 && WK == WK_BF16),
                 "two accumulators only for single CTAs with bf16 weights");
   static constexpr bool kQuant = WK != WK_BF16;
+#ifndef NK_DECODE_KB
+#define NK_DECODE_KB 2
+#endif
+  // K blocks (64 wide) per stage: decode tiles (few token rows, tiny MMAs)
+  // carry two, halving the per-stage hand-offs between the warp roles.
+  static constexpr int kKB = (PAIR == 1 && FA == 1 && BN <= 64 && WK != WK_INT4KN) ? NK_DECODE_KB : 1;
   static constexpr int kATileBytes = 128 * 128;     // 128 weight rows x 64 bf16
-  static constexpr int kABytes = kATileBytes * FA;
+  static constexpr int kABytes = kATileBytes * FA * kKB;
   static constexpr int kBRows = BN / PAIR;          // token rows loaded per CTA
-  static constexpr int kBBytes = kBRows * 128;      // kBRows x 64 bf16
+  static constexpr int kBTileBytes = kBRows * 128;  // kBRows x 64 bf16
+  static constexpr int kBBytes = kBTileBytes * kKB;
   static constexpr int kStageBytes = kABytes + kBBytes;
 #ifndef NK_STAGES_MAX
 #define NK_STAGES_MAX 16

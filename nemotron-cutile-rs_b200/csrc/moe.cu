@@ -26,6 +26,10 @@ struct TileLists {
   int n_out[2];
   TcTile *tiles[2];
   int *count[2];
+  // list 1 (the down projection) with seg_yoff: segment s's rows go to rank
+  // s / seg_per_rank's buffer from row seg_yoff[s] (expert-parallel return)
+  const int32_t *seg_yoff;
+  int seg_per_rank;
 };
 
 __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__restrict__ seg_rows,
@@ -72,6 +76,10 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
     const int fv = n_out - f * fh, tv = rows - t * bn;
     tile.valid = ((fv > fh ? fh : fv) << 16) | (tv > bn ? bn : tv);
     tile.out_col0 = f * fh;
+    if (blockIdx.x == 1 && lists.seg_yoff) {
+      tile.y_rank = seg / lists.seg_per_rank;
+      tile.y_row = lists.seg_yoff[seg] + t * bn;
+    }
     tiles[j] = tile;
   }
 }
@@ -442,10 +450,13 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
 // Grouped expert MLP over R rows laid out as n_seg back-to-back segments:
 // out[r] = relu2(rows[r] · up_eᵀ + b_up) · down_eᵀ + b_down for the segment's
 // expert e.  out may alias rows (rows are fully consumed before out is written).
+// With y_peers, out is unused: segment s's outputs are stored into rank
+// s / seg_per_rank's buffer (y_peers) from row seg_yoff[s] (peer memory).
 nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
                         const int32_t *seg_expert, const int32_t *seg_rows, int n_seg,
                         uint16_t *out, const ExpertsWs &ws, StageTimer &tm, cudaStream_t s,
-                        int max_ctas = 0) {
+                        int max_ctas = 0, const uint64_t *y_peers = nullptr,
+                        const int32_t *seg_yoff = nullptr, int seg_per_rank = 1) {
   const int ctas = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
   int *err = device_error_ptr();
   const int64_t E = L.experts, H = L.hidden, I = L.inter;
@@ -465,6 +476,8 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   lists.tiles[1] = ws.tiles_down;
   lists.count[0] = ws.tile_counts;
   lists.count[1] = ws.tile_counts + 1;
+  lists.seg_yoff = y_peers ? seg_yoff : nullptr;
+  lists.seg_per_rank = seg_per_rank;
   build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, 128 * fa * pair,
                                         lists);
   nk_status st = check_launch("build_tiles_kernel");
@@ -495,6 +508,7 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
     a.ldy = H;
     apply_wop(a, WOp{wk, L.down_w, L.down_scale, L.down_zero_point}, (int)H);
     a.bias = L.down_b;
+    a.y_peers = y_peers;
     st = tc_gemm(wk, L.down_w, E * H, I, w_pitch(wk, I), ws.hmid, R, I, I, kMoeBN, a, gctas, s,
                  pair, fa);
   }
@@ -710,11 +724,12 @@ nk_status moe_forward_ep(nk_ep_ctx *c, const nk_moe_layer &L, const nk_moe_layer
   st = ep_barrier(c, s);  // every routed row has arrived
   if (st != NK_OK) return st;
   uint16_t *recv = ep_recv(c);
+  // the down projection's epilogue stores every result row straight into its
+  // source rank's result buffer (the return exchange fused into the GEMM)
   st = experts_stage(local, recv, c->capacity_rows, c->seg_expert, c->seg_rows,
                      c->ranks * (int)local.experts, recv, ws.x, tm, s,
-                     overlap ? num_sms() - sh_sms : 0);
-  if (st != NK_OK) return st;
-  st = ep_return(c, s);
+                     overlap ? num_sms() - sh_sms : 0, ep_out_table(c), c->ret_off,
+                     (int)local.experts);
   if (st != NK_OK) return st;
   st = ep_barrier(c, s);  // every result is back
   if (st != NK_OK) return st;
