@@ -838,6 +838,50 @@ def nk_arm(args):
         barrier()
         e2e_ms = [e_start.elapsed_time(e_end)]
         pipe.close()
+    elif native:
+        # Native expert parallelism needs no host synchronisation, so the copies
+        # of adjacent steps overlap the forward between them: host->device on
+        # one stream, the forward on the compute stream, device->host on a
+        # third, with two device buffers each for the input and the output.
+        nk.set_stage_timing(False)
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        xins = [torch.empty_like(x), torch.empty_like(x)]
+        outs = [torch.empty_like(out), torch.empty_like(out)]
+        out_hosts = [out_host, torch.empty(T, H, dtype=torch.float32).pin_memory()]
+        copied = [torch.cuda.Event() for _ in range(2)]
+        computed = [torch.cuda.Event() for _ in range(2)]
+        drained = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_steps(n):
+            for i in range(n):
+                b = i % 2
+                if i >= 2:
+                    h2d.wait_event(consumed[b])  # the forward of step i-2 read xins[b]
+                with torch.cuda.stream(h2d):
+                    xins[b].copy_(x_host, non_blocking=True)
+                    copied[b].record(h2d)
+                stream.wait_event(copied[b])
+                if i >= 2:
+                    stream.wait_event(drained[b])  # outs[b] copied out by step i-2
+                ep.forward(xins[b], out=outs[b], indices=idx)
+                consumed[b].record(stream)
+                computed[b].record(stream)
+                d2h.wait_event(computed[b])
+                with torch.cuda.stream(d2h):
+                    out_hosts[b].copy_(outs[b], non_blocking=True)
+                    drained[b].record(d2h)
+
+        e2e_steps(max(args.warmup, 2))
+        barrier()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        h2d.wait_event(e_start)
+        e2e_steps(args.steps)
+        d2h.synchronize()
+        e_end.record(d2h)
+        barrier()
+        e2e_ms = [e_start.elapsed_time(e_end)]
     else:
         e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -935,7 +979,10 @@ def nk_arm(args):
             "nk_moe_pipeline_submit per step (host-buffer executor: pinned x in, f32 out back; "
             "copies of adjacent steps overlap the forward; no L2 flush: each step streams "
             "all routed experts' weights, 1.3-2.6 GB > L2)"
-            if world == 1 else "copy in, forward, copy out back to back per step")
+            if world == 1 else
+            "nk_moe_forward_ep per step with host->device and device->host copies on their own "
+            "streams, overlapping the adjacent steps' forwards (pinned x in, f32 out back)"
+            if native else "copy in, forward, copy out back to back per step")
         if world == 1 and not args.no_gemm_rows:
             line["config1_linear"] = config1_linear(torch, nk, dev)
             line["config2_gemm_rows"] = gemm_sweep(torch, nk, dev, ms=(1, 16, 128, 8192),
