@@ -729,8 +729,57 @@ __global__ void __launch_bounds__(kSelWarps * 32)
     chunk_counts[(int64_t)blockIdx.x * E + e] = hist[e];
 }
 
-__global__ void plan_scan_kernel(int32_t *__restrict__ chunk_counts, int nchunks, int E,
-                                 int32_t *__restrict__ counts, int32_t *__restrict__ offsets);
+// Chunk histograms [nchunks][E] -> each chunk's base per expert (in place)
+// and counts[E]: a block per expert; each thread sums a run of consecutive
+// chunks, a block scan of the run totals, then the runs are written back.
+__global__ void __launch_bounds__(256) chunk_scan_kernel(int32_t *__restrict__ chunk_counts,
+                                                         int nchunks, int E,
+                                                         int32_t *__restrict__ counts) {
+  __shared__ int32_t wsum[8];
+  const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (nchunks + 255) / 256;
+  const int c0 = tid * per, c1 = c0 + per < nchunks ? c0 + per : nchunks;
+  int32_t run = 0;
+  for (int c = c0; c < c1; ++c) run += chunk_counts[(int64_t)c * E + e];
+  int32_t incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  int32_t before = 0;
+  for (int w = 0; w < warp; ++w) before += wsum[w];
+  int32_t base = before + incl - run;
+  for (int c = c0; c < c1; ++c) {
+    const int64_t i = (int64_t)c * E + e;
+    const int32_t v = chunk_counts[i];
+    chunk_counts[i] = base;
+    base += v;
+  }
+  if (tid == 255) counts[e] = before + incl;
+}
+
+// counts[E] -> offsets[E+1] (exclusive scan), one warp.
+__global__ void offsets_scan_kernel(const int32_t *__restrict__ counts, int E,
+                                    int32_t *__restrict__ offsets) {
+  const int lane = threadIdx.x;
+  int32_t carry = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int32_t v = e < E ? counts[e] : 0;
+    int32_t incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (e < E) offsets[e] = carry + incl - v;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) offsets[E] = carry;
+}
 
 // Expert-ordered position of every route slot (offsets[e] + the chunk's base
 // for e + the slot's rank in its chunk); optionally the token row copied there.
@@ -838,10 +887,9 @@ nk_status launch_route_exact(const float *partial, int splits, const uint16_t *x
   st = check_launch("route_select_kernel");
   if (st != NK_OK) return st;
   // chunk histograms -> per-chunk bases (in place), counts, offsets
-  int threads = 32;
-  while (threads < E) threads <<= 1;
-  plan_scan_kernel<<<1, threads, 0, stream>>>(chunk_counts, (int)sel_blocks, E, counts, offsets);
-  st = check_launch("plan_scan_kernel");
+  chunk_scan_kernel<<<(unsigned)E, 256, 0, stream>>>(chunk_counts, (int)sel_blocks, E, counts);
+  offsets_scan_kernel<<<1, 32, 0, stream>>>(counts, E, offsets);
+  st = check_launch("chunk_scan_kernel");
   if (st != NK_OK) return st;
   const int64_t slots = tokens * K;
   const int warps = 8;
