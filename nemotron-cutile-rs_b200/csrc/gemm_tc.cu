@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
   uint64_t *tempty = tfull + 2;     // leader: accumulator set drained (kSlots)
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  unsigned short *epi_stage =
+      reinterpret_cast<unsigned short *>(reinterpret_cast<uint8_t *>(bars) + 768);
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -415,7 +417,38 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
-        if (frow) {
+        // rows bound for a peer: staged through shared memory, 16-byte stores
+        const bool vec_out = tile.y_rank >= 0 && (args.ldy & 7) == 0 &&
+                             sub * 128 + quarter * 32 + 32 <= f_valid;  // warp-uniform
+        if (vec_out) {
+          unsigned short *stg = epi_stage + (warp - 2) * 512;  // [16 tokens][32 features]
+          __nv_bfloat16 *pb = reinterpret_cast<__nv_bfloat16 *>(args.y_peers[tile.y_rank]) +
+                              tile.out_col0 + (int)rank * 128 + sub * 128 + quarter * 32 +
+                              (long long)split * args.split_stride;
+          const int tt = lane >> 1, hh = lane & 1;
+#pragma unroll
+          for (int c = 0; c < BN / 16; ++c) {
+            if (c < chunks) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const uint32_t w = pk[c * 8 + q];
+                stg[(2 * q) * 32 + lane] = (unsigned short)w;
+                stg[(2 * q + 1) * 32 + lane] = (unsigned short)(w >> 16);
+              }
+              __syncwarp();
+              const int j = c * 16 + tt;
+              if (j < t_valid) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(stg + tt * 32 + hh * 16);
+                uint4 *dst = reinterpret_cast<uint4 *>(pb + (long long)(tile.y_row + j) * args.ldy +
+                                                       hh * 16);
+                dst[0] = src[0];
+                dst[1] = src[1];
+              }
+              __syncwarp();
+            }
+          }
+          __threadfence_system();  // peer stores before the next barrier
+        } else if (frow) {
           __nv_bfloat16 *yb = reinterpret_cast<__nv_bfloat16 *>(
                                   tile.y_rank >= 0 ? reinterpret_cast<void *>(args.y_peers[tile.y_rank])
                                                    : args.y) +

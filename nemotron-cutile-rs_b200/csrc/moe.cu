@@ -30,6 +30,9 @@ struct TileLists {
   // s / seg_per_rank's buffer from row seg_yoff[s] (expert-parallel return)
   const int32_t *seg_yoff;
   int seg_per_rank;
+  // list 1 starts at segment seg_rot and wraps: each rank starts its return
+  // at its own rank's rows, so at any time every rank receives from one peer
+  int seg_rot;
 };
 
 __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__restrict__ seg_rows,
@@ -42,9 +45,11 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
   const int n_out = lists.n_out[blockIdx.x];
   TcTile *tiles = lists.tiles[blockIdx.x];
   const int ft = (n_out + fh - 1) / fh;
-  const int c = s < n_seg ? seg_rows[s] : 0;
-  const int mine = ft * ((c + bn - 1) / bn);
-  tiles_sc[s] = mine;
+  const int rot = blockIdx.x == 1 && n_seg > 0 ? lists.seg_rot % n_seg : 0;
+  const int c = s < n_seg ? seg_rows[s] : 0;  // rows scan: segment order
+  const int ps = s < n_seg ? (s + rot < n_seg ? s + rot : s + rot - n_seg) : 0;
+  const int cp = s < n_seg ? seg_rows[ps] : 0;  // tiles scan: list order
+  tiles_sc[s] = ft * ((cp + bn - 1) / bn);
   rows_sc[s] = c;
   __syncthreads();
   for (int o = 1; o < 1024; o <<= 1) {  // inclusive scans of tiles and rows
@@ -64,10 +69,10 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
       if (tiles_sc[mid] > j) hi = mid;
       else lo = mid + 1;
     }
-    const int seg = lo;
+    const int seg = lo + rot < n_seg ? lo + rot : lo + rot - n_seg;
     const int rows = seg_rows[seg];
     const int tt = (rows + bn - 1) / bn;
-    const int local = j - (tiles_sc[seg] - ft * tt);
+    const int local = j - (tiles_sc[lo] - ft * tt);
     const int f = local / tt, t = local - f * tt;
     const int e = seg_expert ? seg_expert[seg] : seg;
     TcTile tile;
@@ -456,7 +461,8 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
                         const int32_t *seg_expert, const int32_t *seg_rows, int n_seg,
                         uint16_t *out, const ExpertsWs &ws, StageTimer &tm, cudaStream_t s,
                         int max_ctas = 0, const uint64_t *y_peers = nullptr,
-                        const int32_t *seg_yoff = nullptr, int seg_per_rank = 1) {
+                        const int32_t *seg_yoff = nullptr, int seg_per_rank = 1,
+                        int seg_rot = 0) {
   const int ctas = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
   int *err = device_error_ptr();
   const int64_t E = L.experts, H = L.hidden, I = L.inter;
@@ -478,6 +484,7 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   lists.count[1] = ws.tile_counts + 1;
   lists.seg_yoff = y_peers ? seg_yoff : nullptr;
   lists.seg_per_rank = seg_per_rank;
+  lists.seg_rot = y_peers ? seg_rot : 0;
   build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, 128 * fa * pair,
                                         lists);
   nk_status st = check_launch("build_tiles_kernel");
@@ -729,7 +736,7 @@ nk_status moe_forward_ep(nk_ep_ctx *c, const nk_moe_layer &L, const nk_moe_layer
   st = experts_stage(local, recv, c->capacity_rows, c->seg_expert, c->seg_rows,
                      c->ranks * (int)local.experts, recv, ws.x, tm, s,
                      overlap ? num_sms() - sh_sms : 0, ep_out_table(c), c->ret_off,
-                     (int)local.experts);
+                     (int)local.experts, c->rank * (int)local.experts);
   if (st != NK_OK) return st;
   st = ep_barrier(c, s);  // every result is back
   if (st != NK_OK) return st;
