@@ -87,8 +87,11 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
   uint64_t *tempty = tfull + 2;     // leader: accumulator set drained (kSlots)
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  // FA == 2 epilogue staging for peer-bound rows: [2][16 tokens][256 features]
   unsigned short *epi_stage =
       reinterpret_cast<unsigned short *>(reinterpret_cast<uint8_t *>(bars) + 768);
+  uint64_t *xbar = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(bars) + 768 +
+                                                2 * 8192);  // buffer b filled by every warp
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -113,6 +116,10 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
       mbar_init(&tempty[b], Cfg::kEpiThreads * PAIR);
     }
     mbar_init(drain, 1);
+    if (FA == 2) {
+      mbar_init(&xbar[0], Cfg::kEpiThreads / 32);
+      mbar_init(&xbar[1], Cfg::kEpiThreads / 32);
+    }
     abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&wmap);
@@ -368,6 +375,7 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
     const int i = sub * 128 + quarter * 32 + lane;  // feature row within this CTA's tile
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t xuse = 0;  // staging buffer uses (peer-bound rows, FA == 2)
     for (int t = cluster_id; t < num_tiles; t += clusters) {
       TcTile tile;
       int k_begin, k_count, split;
@@ -417,37 +425,50 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
-        // rows bound for a peer: staged through shared memory, 16-byte stores
-        const bool vec_out = tile.y_rank >= 0 && (args.ldy & 7) == 0 &&
-                             sub * 128 + quarter * 32 + 32 <= f_valid;  // warp-uniform
-        if (vec_out) {
-          unsigned short *stg = epi_stage + (warp - 2) * 512;  // [16 tokens][32 features]
+        // Rows bound for a peer: each chunk of 16 tokens goes through shared
+        // memory (every warp writes its 32 features), then warp w stores
+        // tokens 2w and 2w+1 as whole rows of up to 256 features (16 bytes
+        // a lane), so NVLink sees full 512-byte runs.  CTA-uniform choice.
+        const bool cta_vec = PAIR == 1 && tile.y_rank >= 0 && (args.ldy & 7) == 0 &&
+                             (f_valid & 7) == 0;
+        if (cta_vec) {
           __nv_bfloat16 *pb = reinterpret_cast<__nv_bfloat16 *>(args.y_peers[tile.y_rank]) +
-                              tile.out_col0 + (int)rank * 128 + sub * 128 + quarter * 32 +
-                              (long long)split * args.split_stride;
-          const int tt = lane >> 1, hh = lane & 1;
+                              tile.out_col0 + (long long)split * args.split_stride;
+          const int ew = warp - 2;
+          const int col = sub * 128 + quarter * 32 + lane;
+          const int nch = (t_valid + 15) >> 4;
+          bool ok = true;
 #pragma unroll
           for (int c = 0; c < BN / 16; ++c) {
-            if (c < chunks) {
+            if (c < nch) {
+              unsigned short *buf = epi_stage + (xuse & 1) * 4096;
+              if (c < chunks) {
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const uint32_t w = pk[c * 8 + q];
-                stg[(2 * q) * 32 + lane] = (unsigned short)w;
-                stg[(2 * q + 1) * 32 + lane] = (unsigned short)(w >> 16);
+                for (int q = 0; q < 8; ++q) {
+                  const uint32_t w = pk[c * 8 + q];
+                  buf[(2 * q) * 256 + col] = (unsigned short)w;
+                  buf[(2 * q + 1) * 256 + col] = (unsigned short)(w >> 16);
+                }
               }
               __syncwarp();
-              const int j = c * 16 + tt;
-              if (j < t_valid) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(stg + tt * 32 + hh * 16);
-                uint4 *dst = reinterpret_cast<uint4 *>(pb + (long long)(tile.y_row + j) * args.ldy +
-                                                       hh * 16);
-                dst[0] = src[0];
-                dst[1] = src[1];
+              if (lane == 0) mbar_arrive(&xbar[xuse & 1]);
+              ok = __all_sync(0xffffffffu, mbar_wait_backoff(&xbar[xuse & 1], (xuse >> 1) & 1, err));
+              ++xuse;
+              if (!ok) break;
+#pragma unroll
+              for (int r = 0; r < 2; ++r) {
+                const int j = c * 16 + 2 * ew + r;
+                if (j < t_valid && lane * 8 < f_valid)
+                  reinterpret_cast<uint4 *>(pb + (long long)(tile.y_row + j) * args.ldy)[lane] =
+                      reinterpret_cast<const uint4 *>(buf + (2 * ew + r) * 256)[lane];
               }
-              __syncwarp();
             }
           }
           __threadfence_system();  // peer stores before the next barrier
+          if (!ok) {
+            *abort_v = 1;
+            break;
+          }
         } else if (frow) {
           __nv_bfloat16 *yb = reinterpret_cast<__nv_bfloat16 *>(
                                   tile.y_rank >= 0 ? reinterpret_cast<void *>(args.y_peers[tile.y_rank])

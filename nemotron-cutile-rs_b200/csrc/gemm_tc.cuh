@@ -144,9 +144,9 @@ struct TcConfig {
   static constexpr int kThreads = 64 + kEpiThreads + kTransformThreads;
   static constexpr int kAccSlots = 2 / FA;          // accumulator sets in TMEM
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  // FA == 2: 1 KB per epilogue warp to stage 16 tokens x 32 features, so
-  // outputs bound for a peer's memory leave as 16-byte stores
-  static constexpr int kEpiStageBytes = FA == 2 ? (kEpiThreads / 32) * 1024 : 0;
+  // FA == 2: two 8 KB buffers of 16 tokens x 256 features (and their two
+  // barriers), so outputs bound for a peer's memory leave as 512-byte rows
+  static constexpr int kEpiStageBytes = FA == 2 ? 2 * 8192 + 64 : 0;
   static constexpr int kSmemBytes =
       1024 + kStages * kStageBytes + kRawSlots * kRawTileBytes + 768 + kEpiStageBytes;
   static constexpr int kFeatRows = 128 * PAIR * FA; // features per output tile
