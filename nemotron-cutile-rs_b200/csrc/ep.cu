@@ -208,14 +208,19 @@ __global__ void ep_dispatch_capped_kernel(const uint4 *__restrict__ x, int64_t s
                                           const int32_t *__restrict__ send_base, int El,
                                           int64_t cap, const uint64_t *__restrict__ peer_recv) {
   const int64_t sl = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (sl >= slots) return;
-  const int e = idx[sl];
-  const int64_t row = (int64_t)send_base[e] + (slot_pos[sl] - offsets[e]);
-  if (row >= cap) return;  // over capacity: reported by ep_capacity_kernel
-  uint4 *dst = reinterpret_cast<uint4 *>(peer_recv[e / El]) + row * row_vecs;
-  const uint4 *src = x + (sl / top_k) * row_vecs;
-  for (int64_t v = threadIdx.x & 31; v < row_vecs; v += 32) dst[v] = src[v];
-  __threadfence_system();  // the owner reads these rows after the next barrier
+  if (sl < slots) {
+    const int e = idx[sl];
+    const int64_t row = (int64_t)send_base[e] + (slot_pos[sl] - offsets[e]);
+    if (row < cap) {  // over capacity: reported by ep_capacity_kernel
+      uint4 *dst = reinterpret_cast<uint4 *>(peer_recv[e / El]) + row * row_vecs;
+      const uint4 *src = x + (sl / top_k) * row_vecs;
+      for (int64_t v = threadIdx.x & 31; v < row_vecs; v += 32) dst[v] = src[v];
+    }
+  }
+  // the owner reads these rows after the next device barrier (a later kernel
+  // on this stream); one system fence per block once its rows are issued
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
 }
 
 nk_status ep_dispatch(nk_ep_ctx *c, const uint16_t *x, int64_t tokens, const int32_t *idx,
