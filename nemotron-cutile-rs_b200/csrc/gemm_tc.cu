@@ -429,11 +429,19 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         // memory (every warp writes its 32 features), then warp w stores
         // tokens 2w and 2w+1 as whole rows of up to 256 features (16 bytes
         // a lane), so NVLink sees full 512-byte runs.  CTA-uniform choice.
-        const bool cta_vec = PAIR == 1 && tile.y_rank >= 0 && (args.ldy & 7) == 0 &&
-                             (f_valid & 7) == 0;
+        // Local outputs take the same path when 16-byte aligned.
+        const bool to_peer = tile.y_rank >= 0;
+        const bool cta_vec =
+            PAIR == 1 && (args.ldy & 7) == 0 && (f_valid & 7) == 0 && (tile.out_col0 & 7) == 0 &&
+            (split == 0 || (args.split_stride & 7) == 0) &&
+            (to_peer || (reinterpret_cast<uintptr_t>(args.y) & 15) == 0);
         if (cta_vec) {
-          __nv_bfloat16 *pb = reinterpret_cast<__nv_bfloat16 *>(args.y_peers[tile.y_rank]) +
-                              tile.out_col0 + (long long)split * args.split_stride;
+          __nv_bfloat16 *pb =
+              reinterpret_cast<__nv_bfloat16 *>(to_peer
+                                                    ? reinterpret_cast<void *>(args.y_peers[tile.y_rank])
+                                                    : args.y) +
+              tile.out_col0 + (long long)split * args.split_stride;
+          const int row0 = to_peer ? tile.y_row : tile.x_row;
           const int ew = warp - 2;
           const int col = sub * 128 + quarter * 32 + lane;
           const int nch = (t_valid + 15) >> 4;
@@ -459,12 +467,12 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
               for (int r = 0; r < 2; ++r) {
                 const int j = c * 16 + 2 * ew + r;
                 if (j < t_valid && lane * 8 < f_valid)
-                  reinterpret_cast<uint4 *>(pb + (long long)(tile.y_row + j) * args.ldy)[lane] =
+                  reinterpret_cast<uint4 *>(pb + (long long)(row0 + j) * args.ldy)[lane] =
                       reinterpret_cast<const uint4 *>(buf + (2 * ew + r) * 256)[lane];
               }
             }
           }
-          __threadfence_system();  // peer stores before the next barrier
+          if (to_peer) __threadfence_system();  // peer stores before the next barrier
           if (!ok) {
             *abort_v = 1;
             break;
