@@ -788,44 +788,26 @@ def nk_arm(args):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     stage_sum = {}
-
-    def read_stages():
-        if world == 1:
-            return nk.moe_stage_times()
-        if native:  # the same marks; between them the exchange phases
-            names = {"router": "router", "route_plan": "route_plan", "gather": "exchange_in",
-                     "up_proj": "up_proj", "down_proj": "down_proj_and_return",
-                     "shared_expert": "shared_wait", "combine": "combine"}
-            return {names[k2]: v for k2, v in nk.moe_stage_times().items()}
-        return ep_timer.step_times()
-
-    # Timed steps: nothing on the host waits for a step (the stage events are
-    # read in a separate pass below), so the launches of step i+1 queue behind
-    # step i as in a serving loop.  The Python-ordered exchanges synchronise
-    # inside each step and read their stage times as they go.
-    per_step_stages = world > 1 and not native
     barrier()
     for i in range(args.steps):
         flush()
         starts[i].record(stream)
         fwd()
         ends[i].record(stream)
-        if per_step_stages:
-            for kname, v in read_stages().items():
-                stage_sum[kname] = stage_sum.get(kname, 0.0) + v
+        if world == 1:
+            times = nk.moe_stage_times()
+        elif native:  # the same marks; between them the exchange phases
+            names = {"router": "router", "route_plan": "route_plan", "gather": "exchange_in",
+                     "up_proj": "up_proj", "down_proj": "down_proj_and_return",
+                     "shared_expert": "shared_wait", "combine": "combine"}
+            times = {names[k2]: v for k2, v in nk.moe_stage_times().items()}
+        else:
+            times = ep_timer.step_times()
+        for kname, v in times.items():
+            stage_sum[kname] = stage_sum.get(kname, 0.0) + v
     barrier()
+
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    stage_steps = args.steps
-    if not per_step_stages:
-        # Stage pass: the same steps again, each read out (host-synchronised)
-        stage_steps = min(args.steps, 20)
-        barrier()
-        for i in range(stage_steps):
-            flush()
-            fwd()
-            for kname, v in read_stages().items():
-                stage_sum[kname] = stage_sum.get(kname, 0.0) + v
-        barrier()
 
     # e2e: host (pinned) input -> device -> forward -> host output, every step.
     # One GPU: through the host-buffer executor (nk_moe_pipeline_*), whose
@@ -920,12 +902,12 @@ def nk_arm(args):
     total_e2e = sum(e2e_ms)
     if world == 1:  # up/down stages; the shared expert runs beside them when overlapped
         grouped_ms = (stage_sum.get("up_proj", 0.0) + stage_sum.get("down_proj", 0.0) +
-                      stage_sum.get("shared_expert", 0.0)) / stage_steps
+                      stage_sum.get("shared_expert", 0.0)) / args.steps
     elif native:  # the down stage includes the return exchange and its barrier
         grouped_ms = (stage_sum.get("up_proj", 0.0) +
-                      stage_sum.get("down_proj_and_return", 0.0)) / stage_steps
+                      stage_sum.get("down_proj_and_return", 0.0)) / args.steps
     else:
-        grouped_ms = stage_sum.get("experts", 0.0) / stage_steps
+        grouped_ms = stage_sum.get("experts", 0.0) / args.steps
     if world > 1:
         t = torch.tensor([total_ms, total_e2e, grouped_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -969,10 +951,7 @@ def nk_arm(args):
             "tflops": (routed + shared + router) * world * args.steps / (total_ms / 1e3) / 1e12,
             "tensor_frac_of_measured": ((routed + shared + router) / (total_ms / args.steps / 1e3)
                                         / 1e12) / pk["bf16_tflops"],
-            "stages_ms": {k2: v / stage_steps for k2, v in stage_sum.items()},
-            "stages_how": (f"CUDA events between the forward's stages, read after each of "
-                           f"{stage_steps} steps run after the timed ones"
-                           if not per_step_stages else "read after each timed step"),
+            "stages_ms": {k2: v / args.steps for k2, v in stage_sum.items()},
             "roofline": {
                 "kernel": ("tc_gemm_kernel: grouped expert up/down projections with the shared "
                            "expert's two GEMMs running beside them (4 launches per step)"
