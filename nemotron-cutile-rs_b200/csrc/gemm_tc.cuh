@@ -149,6 +149,7 @@ struct TcConfig {
   static constexpr int kEpiStageBytes = FA == 2 ? 2 * 8192 + 64 : 0;
   static constexpr int kSmemBytes =
       1024 + kStages * kStageBytes + kRawSlots * kRawTileBytes + 768 + kEpiStageBytes;
+  static_assert(kSmemBytes <= 232448, "dynamic shared memory above the sm_100a limit");
   static constexpr int kFeatRows = 128 * PAIR * FA; // features per output tile
 };
 
