@@ -30,7 +30,9 @@ namespace nk {
 __global__ void ep_plan_kernel(const int32_t *__restrict__ C, int G, int E, int me, int phases,
                                int64_t cap, int32_t *__restrict__ send_base,
                                int32_t *__restrict__ seg_rows, int32_t *__restrict__ rstart,
-                               int32_t *__restrict__ yoff, int32_t *__restrict__ total) {
+                               int32_t *__restrict__ yoff, int32_t *__restrict__ total,
+                               int32_t *__restrict__ pull_tab = nullptr,
+                               int32_t *__restrict__ arrived = nullptr) {
   const int El = E / G, Elh = El / phases;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int g = e / El, j = e % El, h = j / Elh, jj = j % Elh;
@@ -61,6 +63,20 @@ __global__ void ep_plan_kernel(const int32_t *__restrict__ C, int G, int E, int 
       }
     }
     total[0] = all;
+    if (pull_tab && phases == 1) {
+      // segment (s, j): rows contiguous in source s's send buffer (expert
+      // order, from yoff) and in this receive buffer (from rstart); clipped
+      // to the receive capacity (the excess is reported by ep_capacity_kernel)
+      for (int g = 0; g < G * El; ++g) {
+        int rows = seg_rows[g];
+        const int64_t room = cap - (int64_t)rstart[g];
+        if ((int64_t)rows > room) rows = room > 0 ? (int)room : 0;
+        pull_tab[g * 3 + 0] = yoff[g];
+        pull_tab[g * 3 + 1] = rstart[g];
+        pull_tab[g * 3 + 2] = rows;
+        arrived[g] = 0;
+      }
+    }
   }
 }
 
@@ -164,6 +180,10 @@ __global__ void ep_capacity_kernel(int32_t *total, int64_t cap, int *err) {
 
 static uint64_t *table(const nk_ep_ctx *c, int which) { return c->tables + which * c->ranks; }
 const uint64_t *ep_out_table(const nk_ep_ctx *c) { return table(c, 1); }
+const uint64_t *ep_send_table(const nk_ep_ctx *c) { return table(c, 4); }
+uint16_t *ep_send(const nk_ep_ctx *c) {
+  return reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(c->block) + c->off_send);
+}
 
 uint16_t *ep_recv(const nk_ep_ctx *c) { return reinterpret_cast<uint16_t *>(c->block); }
 uint16_t *ep_out(const nk_ep_ctx *c) {
@@ -192,9 +212,9 @@ nk_status ep_barrier(nk_ep_ctx *c, cudaStream_t s) {
 }
 
 nk_status ep_plan(nk_ep_ctx *c, cudaStream_t s) {
-  ep_plan_kernel<<<1, 256, 0, s>>>(ep_counts_all(c), c->ranks, (int)c->experts, c->rank, 1, 0,
-                                   c->send_base, c->seg_rows, c->seg_start, c->ret_off,
-                                   c->total);
+  ep_plan_kernel<<<1, 256, 0, s>>>(ep_counts_all(c), c->ranks, (int)c->experts, c->rank, 1,
+                                   c->capacity_rows, c->send_base, c->seg_rows, c->seg_start,
+                                   c->ret_off, c->total, c->pull_tab, c->arrived);
   nk_status st = check_launch("ep_plan_kernel");
   if (st != NK_OK) return st;
   ep_capacity_kernel<<<1, 32, 0, s>>>(c->total, c->capacity_rows, device_error_ptr());
@@ -391,7 +411,8 @@ nk_status nk_ep_create(int32_t ranks, int32_t rank, int64_t experts, int64_t hid
   c->off_out = al((size_t)capacity_rows * hidden * 2);
   c->off_counts = c->off_out + al((size_t)max_tokens * top_k * hidden * 2);
   c->off_flags = c->off_counts + al((size_t)ranks * experts * 4);
-  c->block_bytes = c->off_flags + al((size_t)ranks * 4);
+  c->off_send = c->off_flags + al((size_t)ranks * 4);
+  c->block_bytes = c->off_send + al((size_t)max_tokens * top_k * hidden * 2);
   const int El = (int)(experts / ranks);
   auto cleanup = [&](nk_status st) {
     if (c->block) cudaFree(c->block);
@@ -403,17 +424,19 @@ nk_status nk_ep_create(int32_t ranks, int32_t rank, int64_t experts, int64_t hid
   cudaError_t e = cudaMalloc(&c->block, c->block_bytes);
   if (e != cudaSuccess) return cleanup(fail_cuda(e, "cudaMalloc(ep block)"));
   e = cudaMemset(c->block, 0, c->block_bytes);  // flags start at epoch 0
-  if (e == cudaSuccess) e = cudaMalloc(&c->tables, sizeof(uint64_t) * 4 * ranks);
+  if (e == cudaSuccess) e = cudaMalloc(&c->tables, sizeof(uint64_t) * 5 * ranks);
   // plan arrays in one allocation
   const size_t nseg = (size_t)ranks * El;
   if (e == cudaSuccess)
-    e = cudaMalloc(&c->send_base, sizeof(int32_t) * (experts + 5 * nseg + 1));
+    e = cudaMalloc(&c->send_base, sizeof(int32_t) * (experts + 9 * nseg + 1));
   if (e != cudaSuccess) return cleanup(fail_cuda(e, "cudaMalloc(ep plan)"));
   c->seg_rows = c->send_base + experts;
   c->seg_start = c->seg_rows + nseg;
   c->ret_off = c->seg_start + nseg;
   c->seg_expert = c->ret_off + nseg;
   c->total = c->seg_expert + nseg;
+  c->pull_tab = c->total + 1;
+  c->arrived = c->pull_tab + 3 * nseg;
   {  // segment order [source rank][local expert]
     int32_t *h = new int32_t[nseg];
     for (size_t i = 0; i < nseg; ++i) h[i] = (int32_t)(i % El);
@@ -437,7 +460,7 @@ nk_status nk_ep_connect(nk_ep_ctx *c, const void *all_blobs) {
   if (!c || !all_blobs) return fail(NK_INVALID_PARAMS, "ctx and blobs");
   if (c->connected) return fail(NK_INVALID_PARAMS, "already connected");
   const nk_ep_blob *b = reinterpret_cast<const nk_ep_blob *>(all_blobs);
-  uint64_t h[4 * 64];
+  uint64_t h[5 * 64];
   for (int p = 0; p < c->ranks; ++p) {
     if (b[p].magic != 0x4e4b4550u || (int)b[p].rank != p || (int)b[p].ranks != c->ranks ||
         b[p].block_bytes != c->block_bytes)
@@ -456,8 +479,9 @@ nk_status nk_ep_connect(nk_ep_ctx *c, const void *all_blobs) {
     h[1 * c->ranks + p] = reinterpret_cast<uint64_t>(base + c->off_out);
     h[2 * c->ranks + p] = reinterpret_cast<uint64_t>(base + c->off_counts);
     h[3 * c->ranks + p] = reinterpret_cast<uint64_t>(base + c->off_flags);
+    h[4 * c->ranks + p] = reinterpret_cast<uint64_t>(base + c->off_send);
   }
-  NK_CUDA_TRY(cudaMemcpy(c->tables, h, sizeof(uint64_t) * 4 * c->ranks, cudaMemcpyHostToDevice));
+  NK_CUDA_TRY(cudaMemcpy(c->tables, h, sizeof(uint64_t) * 5 * c->ranks, cudaMemcpyHostToDevice));
   c->connected = true;
   return ok();
 }

@@ -208,6 +208,14 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
         TcTile tile;
         int k_begin, k_count, split;
         load_tile<BN, FH>(args, t, tile, k_begin, k_count, split);
+        if (FA == 2 && args.pull_tab && tile.src >= 0) {
+          if (*abort_v || !wait_count_geq(args.pull_arrived + tile.src,
+                                          args.pull_tab[tile.src * 3 + 2], err)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();  // the copy warps' stores, before our TMA reads
+        }
         const uint32_t n_mma = mma_n(tile.valid & 0xFFFF, BN);
         const int a_row = tile.w_row + (int)rank * 128;
         const int n_a = FA == 2 && (tile.valid >> 16) > 128 ? 2 : 1;  // weight tiles loaded
@@ -533,6 +541,52 @@ __global__ void __launch_bounds__(TcConfig<WK, BN, PAIR, FA>::kThreads, 1)
       if (++acc == kSlots) {
         acc = 0;
         acc_phase ^= 1;
+      }
+    }
+  } else if (FA == 2) {
+    // ------------------------------------------------------------ copy warps
+    // In-kernel pull: jobs of up to 4 rows, numbered through the segments in
+    // the order pull_rot, pull_rot + 1, ...; job j goes to copy warp j mod
+    // (CTAs x copy warps), so all CTAs work on the first segments first.
+    if (args.pull_tab) {
+      const int NS = args.pull_segs;
+      const int nw = gridDim.x * Cfg::kCopyWarps;
+      const int gw = (warp - 2 - kEpiWarps) * gridDim.x + blockIdx.x;
+      const long long rv = args.pull_row_vecs;
+      constexpr int kJobRows = 4, kUnroll = 16;
+      int p = 0, g = args.pull_rot % NS, jbase = 0;
+      int rows_g = args.pull_tab[g * 3 + 2];
+      int jobs_g = (rows_g + kJobRows - 1) / kJobRows;
+      for (int job = gw;; job += nw) {
+        while (p < NS && job - jbase >= jobs_g) {
+          jbase += jobs_g;
+          if (++p < NS) {
+            g = args.pull_rot + p < NS ? args.pull_rot + p : args.pull_rot + p - NS;
+            rows_g = args.pull_tab[g * 3 + 2];
+            jobs_g = (rows_g + kJobRows - 1) / kJobRows;
+          }
+        }
+        if (p >= NS || *abort_v) break;
+        const int r0 = (job - jbase) * kJobRows;
+        const int nr = rows_g - r0 < kJobRows ? rows_g - r0 : kJobRows;
+        const uint4 *src =
+            reinterpret_cast<const uint4 *>(args.pull_src[g / args.pull_seg_per_rank]) +
+            (long long)(args.pull_tab[g * 3 + 0] + r0) * rv;
+        uint4 *dst = reinterpret_cast<uint4 *>(args.pull_dst) +
+                     (long long)(args.pull_tab[g * 3 + 1] + r0) * rv;
+        const long long n = nr * rv;
+        for (long long v = lane; v < n; v += 32 * kUnroll) {
+          uint4 tmp[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u)
+            if (v + u * 32 < n) tmp[u] = src[v + u * 32];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u)
+            if (v + u * 32 < n) dst[v + u * 32] = tmp[u];
+        }
+        __threadfence();  // this lane's stores, before the warp's count
+        __syncwarp();
+        if (lane == 0) atomicAdd(args.pull_arrived + g, nr);
       }
     }
   } else if (kQuant) {

@@ -42,6 +42,7 @@ struct TcTile {  // one output tile: 128 (256 for CTA pairs) features x up to BN
   int out_col0;    // output column of feature 0 of the tile
   int y_row = 0;   // y_rank >= 0: output row of token 0 in rank y_rank's buffer
   int y_rank = -1; // -1: output row x_row + j of args.y
+  int src = -1;    // >= 0: segment whose rows this launch pulls in (args.pull_tab)
 };
 
 struct TcArgs {
@@ -70,6 +71,19 @@ struct TcArgs {
   const float *group_scale; // [groups] or null
   const uint8_t *group_zp;  // [groups] or null (w_zero_point then)
   int group_rows;
+  // In-kernel pull of routed rows (expert parallel, FA == 2 kernels): copy
+  // warps in every CTA copy each receive segment's rows from its source
+  // rank's send buffer (peer memory) into the receive buffer, segments in the
+  // order pull_rot, pull_rot + 1, ... (mod pull_segs), and add the rows they
+  // copied to pull_arrived[segment].  The producer starts a tile with
+  // src >= 0 (its segment) only once that segment's rows have all arrived.
+  const uint64_t *pull_src; // [ranks] send buffers (bf16 rows); segment g's
+  int pull_seg_per_rank;    //   source rank is g / pull_seg_per_rank
+  const int32_t *pull_tab;  // [segments][3]: first send row, first receive row, rows
+  int *pull_arrived;        // [segments] rows arrived; zero before the launch
+  void *pull_dst;           // receive buffer (bf16 rows)
+  int pull_segs, pull_rot;
+  long long pull_row_vecs;  // 16-byte words per row
   int *err;
 };
 
@@ -141,7 +155,9 @@ struct TcConfig {
 #endif
   static constexpr int kTransformThreads = kQuant ? NK_TRANSFORM_THREADS : 0;
   static constexpr int kEpiThreads = 128 * FA;      // 4 warps per accumulator
-  static constexpr int kThreads = 64 + kEpiThreads + kTransformThreads;
+  // FA == 2: two copy warps for the in-kernel pull (idle without one)
+  static constexpr int kCopyWarps = FA == 2 ? 2 : 0;
+  static constexpr int kThreads = 64 + kEpiThreads + kTransformThreads + 32 * kCopyWarps;
   static constexpr int kAccSlots = 2 / FA;          // accumulator sets in TMEM
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   // FA == 2: two 8 KB buffers of 16 tokens x 256 features (and their two

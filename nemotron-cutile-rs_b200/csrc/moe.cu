@@ -33,6 +33,9 @@ struct TileLists {
   // list 1 starts at segment seg_rot and wraps: each rank starts its return
   // at its own rank's rows, so at any time every rank receives from one peer
   int seg_rot;
+  // list 0 (the up projection) of an in-kernel pull: the same rotation, and
+  // each tile carries its segment (whose rows it waits for)
+  int pull;
 };
 
 __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__restrict__ seg_rows,
@@ -45,7 +48,7 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
   const int n_out = lists.n_out[blockIdx.x];
   TcTile *tiles = lists.tiles[blockIdx.x];
   const int ft = (n_out + fh - 1) / fh;
-  const int rot = blockIdx.x == 1 && n_seg > 0 ? lists.seg_rot % n_seg : 0;
+  const int rot = n_seg > 0 && (blockIdx.x == 1 || lists.pull) ? lists.seg_rot % n_seg : 0;
   const int c = s < n_seg ? seg_rows[s] : 0;  // rows scan: segment order
   const int ps = s < n_seg ? (s + rot < n_seg ? s + rot : s + rot - n_seg) : 0;
   const int cp = s < n_seg ? seg_rows[ps] : 0;  // tiles scan: list order
@@ -85,6 +88,7 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t *__rest
       tile.y_rank = seg / lists.seg_per_rank;
       tile.y_row = lists.seg_yoff[seg] + t * bn;
     }
+    if (blockIdx.x == 0 && lists.pull) tile.src = seg;
     tiles[j] = tile;
   }
 }
@@ -362,6 +366,16 @@ int grouped_fa() {
   return v;
 }
 
+// Expert parallel, bf16 experts: the owners pull routed rows inside their up
+// projection (default); NK_EP_PULL=0 pushes them before it instead.
+bool ep_pull_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("NK_EP_PULL");
+    return !(e && atoi(e) == 0);
+  }();
+  return v;
+}
+
 // CTA pairs for the grouped GEMMs: NK_GROUPED_PAIR=2 selects them (default
 // single CTAs).
 int grouped_pair() {
@@ -457,12 +471,19 @@ nk_status dispatch_stage(const nk_moe_layer &L, const uint16_t *x, int64_t T, in
 // expert e.  out may alias rows (rows are fully consumed before out is written).
 // With y_peers, out is unused: segment s's outputs are stored into rank
 // s / seg_per_rank's buffer (y_peers) from row seg_yoff[s] (peer memory).
+// With pull (bf16 experts, two-accumulator kernel), the up projection's copy
+// warps first bring each source rank's rows into `rows` (the receive buffer).
+struct EpPull {
+  const uint64_t *src;  // [ranks] send buffers
+  const int32_t *tab;   // [segments][3] first send row, first receive row, rows
+  int *arrived;         // [segments], zeroed by the plan
+};
 nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
                         const int32_t *seg_expert, const int32_t *seg_rows, int n_seg,
                         uint16_t *out, const ExpertsWs &ws, StageTimer &tm, cudaStream_t s,
                         int max_ctas = 0, const uint64_t *y_peers = nullptr,
                         const int32_t *seg_yoff = nullptr, int seg_per_rank = 1,
-                        int seg_rot = 0) {
+                        int seg_rot = 0, const EpPull *pull = nullptr) {
   const int ctas = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
   int *err = device_error_ptr();
   const int64_t E = L.experts, H = L.hidden, I = L.inter;
@@ -475,6 +496,7 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   const int pair = gp == 2 ? 2 : 1;
   const int fa = wk == WK_BF16 && pair == 1 ? grouped_fa() : 1;
   const int gctas = pair == 2 ? (ctas & ~1) : ctas;
+  if (pull && fa != 2) return fail(NK_UNSUPPORTED, "in-kernel pull needs the two-accumulator kernel");
   TileLists lists;
   lists.n_out[0] = (int)I;
   lists.n_out[1] = (int)H;
@@ -484,7 +506,8 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
   lists.count[1] = ws.tile_counts + 1;
   lists.seg_yoff = y_peers ? seg_yoff : nullptr;
   lists.seg_per_rank = seg_per_rank;
-  lists.seg_rot = y_peers ? seg_rot : 0;
+  lists.seg_rot = y_peers || pull ? seg_rot : 0;
+  lists.pull = pull ? 1 : 0;
   build_tiles_kernel<<<2, 1024, 0, s>>>(seg_rows, seg_expert, n_seg, kMoeBN, 128 * fa * pair,
                                         lists);
   nk_status st = check_launch("build_tiles_kernel");
@@ -501,6 +524,16 @@ nk_status experts_stage(const nk_moe_layer &L, const uint16_t *rows, int64_t R,
     apply_wop(a, WOp{wk, L.up_w, L.up_scale, L.up_zero_point}, (int)I);
     a.bias = L.up_b;
     a.relu2 = 1;
+    if (pull) {
+      a.pull_src = pull->src;
+      a.pull_tab = pull->tab;
+      a.pull_arrived = pull->arrived;
+      a.pull_dst = const_cast<uint16_t *>(rows);
+      a.pull_seg_per_rank = seg_per_rank;
+      a.pull_segs = n_seg;
+      a.pull_rot = seg_rot;
+      a.pull_row_vecs = H / 8;
+    }
     st = tc_gemm(wk, L.up_w, E * I, H, w_pitch(wk, H), rows, R, H, H, kMoeBN, a, gctas, s, pair,
                  fa);
     if (st != NK_OK) return st;
@@ -720,23 +753,34 @@ nk_status moe_forward_ep(nk_ep_ctx *c, const nk_moe_layer &L, const nk_moe_layer
     if (st != NK_OK) return st;
     NK_CUDA_TRY(cudaEventRecord(side->join, side->stream));
   }
-  st = dispatch_stage(L, x, T, idx, rw, ws.counts, ws.offsets, ws.slot_pos, nullptr, ws.d, tm, s);
+  // bf16 experts: the owners pull the routed rows inside their up projection
+  // (the routing writes them in expert order into this rank's send buffer);
+  // otherwise they are pushed to the owners before it (ep_dispatch + barrier)
+  const bool pull = ep_pull_enabled() && moe_wk(local) == WK_BF16 && grouped_pair() == 1 &&
+                    grouped_fa() == 2;
+  st = dispatch_stage(L, x, T, idx, rw, ws.counts, ws.offsets, ws.slot_pos,
+                      pull ? ep_send(c) : nullptr, ws.d, tm, s);
   if (st != NK_OK) return st;
-  st = ep_exchange_counts(c, ws.counts, s);  // also: every peer is done with the last forward
+  // also: every peer is done with the last forward, and (pull) every send
+  // buffer of this forward is written
+  st = ep_exchange_counts(c, ws.counts, s);
   if (st != NK_OK) return st;
   st = ep_plan(c, s);
   if (st != NK_OK) return st;
-  st = ep_dispatch(c, x, T, idx, ws.slot_pos, ws.offsets, s);
-  if (st != NK_OK) return st;
-  st = ep_barrier(c, s);  // every routed row has arrived
-  if (st != NK_OK) return st;
+  if (!pull) {
+    st = ep_dispatch(c, x, T, idx, ws.slot_pos, ws.offsets, s);
+    if (st != NK_OK) return st;
+    st = ep_barrier(c, s);  // every routed row has arrived
+    if (st != NK_OK) return st;
+  }
   uint16_t *recv = ep_recv(c);
+  const EpPull pl{ep_send_table(c), c->pull_tab, c->arrived};
   // the down projection's epilogue stores every result row straight into its
   // source rank's result buffer (the return exchange fused into the GEMM)
   st = experts_stage(local, recv, c->capacity_rows, c->seg_expert, c->seg_rows,
                      c->ranks * (int)local.experts, recv, ws.x, tm, s,
                      overlap ? num_sms() - sh_sms : 0, ep_out_table(c), c->ret_off,
-                     (int)local.experts, c->rank * (int)local.experts);
+                     (int)local.experts, c->rank * (int)local.experts, pull ? &pl : nullptr);
   if (st != NK_OK) return st;
   st = ep_barrier(c, s);  // every result is back
   if (st != NK_OK) return st;

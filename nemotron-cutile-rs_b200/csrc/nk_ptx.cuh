@@ -113,6 +113,36 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   return v;
 }
 
+// Global-memory writes made visible by an acquire -> ordered before this
+// thread's later async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *count >= need (acquire): false, with NK_TIMEOUT in
+// *err, after NK_WAIT_LIMIT_NS or once another role recorded an error.
+__device__ __forceinline__ bool wait_count_geq(const int *count, int need, int *err) {
+  if (ld_acquire_gpu(count) >= need) return true;
+  const uint64_t t0 = nk_globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(count) >= need) return true;
+    if ((it & 63u) == 0) {
+      if (nk_globaltimer() - t0 > NK_WAIT_LIMIT_NS) {
+        atomicCAS(err, 0, NK_TIMEOUT);
+        return false;
+      }
+      if (*(volatile int *)err != 0) return false;
+    }
+  }
+}
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (tensor core).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -1,7 +1,8 @@
 """Expert parallelism on 2 B200s: each rank owns half of the experts, routes
 its own tokens and exchanges routed rows with the other rank.  Every
 exchange — the native C-ABI executor (nk_moe_forward_ep: counts, rows and
-results moved by libnk kernels over NVLink peer memory, device barriers), the
+results moved by libnk kernels over NVLink peer memory, device barriers; rows
+pulled by the owners' up projection or pushed before it), the
 Python-orchestrated peer-store exchange and NCCL all-to-all-v — must
 reproduce the oracle's MoeLayer::forward_into restatement (moe.rs:154-249) on
 the rank's own tokens: routing indices bit-exact, outputs within the bf16 bar
@@ -46,7 +47,9 @@ def _worker(rank, world, port, q, mode):
                          shared_down_w=rn(H, Is).bfloat16())
     local = local_layer(full, rank, world)
     tmax = T + 37 * world
-    if mode == "native":
+    if mode == "native_push":  # rows pushed to their owners before the up projection
+        os.environ["NK_EP_PULL"] = "0"
+    if mode.startswith("native"):
         ep = NativeExpertParallelMoe(full, local, max_tokens=tmax)
     else:
         be = NkBackend(full, local)
@@ -77,9 +80,9 @@ def _worker(rank, world, port, q, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["native", "peer", "peer2", "nccl"],
-                         ids=["native_c_abi", "nvlink_peer_stores", "nvlink_peer_stores_2_phases",
-                              "nccl_all_to_all"])
+@pytest.mark.parametrize("mode", ["native", "native_push", "peer", "peer2", "nccl"],
+                         ids=["native_c_abi_pull", "native_c_abi_push", "nvlink_peer_stores",
+                              "nvlink_peer_stores_2_phases", "nccl_all_to_all"])
 def test_expert_parallel_two_gpus_matches_oracle(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
