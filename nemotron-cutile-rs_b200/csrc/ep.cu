@@ -211,10 +211,11 @@ nk_status ep_barrier(nk_ep_ctx *c, cudaStream_t s) {
   return check_launch("ep_barrier_kernel");
 }
 
-nk_status ep_plan(nk_ep_ctx *c, cudaStream_t s) {
+nk_status ep_plan(nk_ep_ctx *c, cudaStream_t s, bool pull) {
   ep_plan_kernel<<<1, 256, 0, s>>>(ep_counts_all(c), c->ranks, (int)c->experts, c->rank, 1,
                                    c->capacity_rows, c->send_base, c->seg_rows, c->seg_start,
-                                   c->ret_off, c->total, c->pull_tab, c->arrived);
+                                   c->ret_off, c->total, pull ? c->pull_tab : nullptr,
+                                   c->arrived);
   nk_status st = check_launch("ep_plan_kernel");
   if (st != NK_OK) return st;
   ep_capacity_kernel<<<1, 32, 0, s>>>(c->total, c->capacity_rows, device_error_ptr());

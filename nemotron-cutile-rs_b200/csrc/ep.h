@@ -32,7 +32,8 @@ nk_status ep_exchange_counts(nk_ep_ctx *c, const int32_t *counts, cudaStream_t s
 // Device barrier across the ranks: every rank's prior stores on its stream
 // are visible to all before any rank continues.  Bounded (NK_TIMEOUT).
 nk_status ep_barrier(nk_ep_ctx *c, cudaStream_t s);
-nk_status ep_plan(nk_ep_ctx *c, cudaStream_t s);
+// pull: also the per-segment pull table and zeroed arrival counts
+nk_status ep_plan(nk_ep_ctx *c, cudaStream_t s, bool pull);
 nk_status ep_dispatch(nk_ep_ctx *c, const uint16_t *x, int64_t tokens, const int32_t *idx,
                       const int32_t *slot_pos, const int32_t *offsets, cudaStream_t s);
 nk_status ep_return(nk_ep_ctx *c, cudaStream_t s);

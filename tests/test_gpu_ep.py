@@ -47,8 +47,8 @@ def _worker(rank, world, port, q, mode):
                          shared_down_w=rn(H, Is).bfloat16())
     local = local_layer(full, rank, world)
     tmax = T + 37 * world
-    if mode == "native_push":  # rows pushed to their owners before the up projection
-        os.environ["NK_EP_PULL"] = "0"
+    if mode == "native_pull":  # rows pulled by the owners' up projection
+        os.environ["NK_EP_PULL"] = "1"
     if mode.startswith("native"):
         ep = NativeExpertParallelMoe(full, local, max_tokens=tmax)
     else:
@@ -80,8 +80,8 @@ def _worker(rank, world, port, q, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["native", "native_push", "peer", "peer2", "nccl"],
-                         ids=["native_c_abi_pull", "native_c_abi_push", "nvlink_peer_stores",
+@pytest.mark.parametrize("mode", ["native", "native_pull", "peer", "peer2", "nccl"],
+                         ids=["native_c_abi_push", "native_c_abi_pull", "nvlink_peer_stores",
                               "nvlink_peer_stores_2_phases", "nccl_all_to_all"])
 def test_expert_parallel_two_gpus_matches_oracle(mode):
     if torch.cuda.device_count() < 2:
