@@ -498,6 +498,11 @@ nk_status nk_ep_return_segments(const uint16_t *expert_rows, int64_t hidden, int
  *      no library collective; the barriers are flag words in peer memory,
  *      each wait bounded (NK_TIMEOUT in nk_device_status when a peer does not
  *      arrive within 2 s).  Plain peer loads and stores only (no multicast).
+ *      The down projection's epilogue stores the results straight into the
+ *      source ranks' buffers (no separate return kernel).  With the
+ *      environment variable NK_EP_PULL=1 and bf16 experts, the routed rows
+ *      are instead pulled by the owners' up projection from the sources' send
+ *      buffers (no dispatch kernel, no barrier before the experts).
  *   4. nk_ep_destroy after every rank has finished its last forward (for
  *      example after nk_ep_barrier and a stream synchronisation).
  *
